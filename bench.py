@@ -1,0 +1,488 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Paged-attention decode benchmark (one JSON line on rank 0).
+
+Workload (default): continuous-batching decode at Llama-3-8B attention shape,
+32 q / 8 kv heads, head_dim 128, 32 layers, MX-FP8 KV in 16-token pages,
+256 requests with log-uniform contexts in [128, 16384], blocks scattered over
+an arena. One step = the 32 layers' decode attention of every request (one
+launch per layer, as a model runs it). Requests are sharded over N GPUs by
+longest-processing-time packing, with no communication (strong scaling:
+the batch is fixed).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kllm|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+--impl reference times the reference's own CPU attention
+(userspace/compute/ace_attention.c, built from its sources into oracle/_ref)
+on the host cores over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "xpu-kllm_b200"))
+
+from kllm_b200 import workloads as wl  # noqa: E402
+
+METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200"
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def lpt_shard(lens: np.ndarray, n: int) -> list[list[int]]:
+    """Longest-processing-time packing of requests onto n ranks."""
+    loads = [0] * n
+    out: list[list[int]] = [[] for _ in range(n)]
+    for s in np.argsort(-lens, kind="stable"):
+        r = int(np.argmin(loads))
+        out[r].append(int(s))
+        loads[r] += int(lens[s])
+    return [sorted(x) for x in out]
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+class DecodeRig:
+    """The rank's requests resident on its GPU: pages, table, Q, outputs."""
+
+    def __init__(self, cfg: wl.DecodeConfig, seqs: list[int], all_lens: np.ndarray, be,
+                 torch, device: int, seed: int = 0, arena_factor: float = 1.25):
+        self.cfg, self.be, self.torch = cfg, be, torch
+        self.seqs = seqs
+        self.lens = all_lens[seqs].astype(np.int32)
+        c = cfg
+        self.B = len(seqs)
+        dev = torch.device("cuda", device)
+        pages = (self.lens.astype(np.int64) + c.block - 1) // c.block
+        need = int(pages.sum())
+        free, _ = torch.cuda.mem_get_info(device)
+        slot_b = c.slot_bytes()
+        want = int(math.ceil(need * arena_factor))
+        cap = int((free * 0.85 - 4e9) // slot_b)
+        n_slots = max(need, min(want, cap))
+        self.arena_bytes = n_slots * slot_b
+        self.plan = wl.plan_pages(c, self.lens, seed, n_slots=n_slots)
+        self.arena = torch.empty(self.arena_bytes, dtype=torch.uint8, device=dev)
+        table = wl.block_table(self.plan, c, self.arena.data_ptr())
+        self.table = torch.from_numpy(table.view(np.uint8).copy()).to(dev)
+        self.seq_lens = torch.from_numpy(self.lens.copy()).to(dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000003 + 17)
+        mult = torch.from_numpy(wl.magnitudes(c, seed)[seqs].astype(np.float32)).to(dev)
+        self.q = torch.randn((c.layers, self.B, c.hq, c.d), generator=g, device=dev,
+                             dtype=torch.float32).to(torch.bfloat16)
+        self.out = torch.zeros((c.layers, self.B, c.hq, c.d), dtype=torch.bfloat16, device=dev)
+        self._fill(g, mult, dev)
+
+    def _fill(self, g, mult, dev):
+        """Quantize-on-write of every context token through the append ABI."""
+        torch, c = self.torch, self.cfg
+        st = torch.cuda.current_stream().cuda_stream
+        chunk = 1 << 17
+        tok_seq = np.concatenate([np.full(L, i, np.int32) for i, L in enumerate(self.lens)])
+        tok_pos = np.concatenate([np.arange(L, dtype=np.int32) for L in self.lens])
+        ts_all = torch.from_numpy(tok_seq).to(dev)
+        tp_all = torch.from_numpy(tok_pos).to(dev)
+        for layer in range(c.layers):
+            for a in range(0, len(tok_seq), chunk):
+                b = min(a + chunk, len(tok_seq))
+                ts, tp = ts_all[a:b], tp_all[a:b]
+                m = mult[ts.long()][:, :, None]
+                k = (torch.randn((b - a, c.hkv, c.d), generator=g, device=dev) * m).to(
+                    torch.bfloat16)
+                v = (torch.randn((b - a, c.hkv, c.d), generator=g, device=dev) * m).to(
+                    torch.bfloat16)
+                rc = self.be.append(k=k.data_ptr(), v=v.data_ptr(), token_seq=ts.data_ptr(),
+                                    token_pos=tp.data_ptr(), num_tokens=b - a,
+                                    block_tables=self.table.data_ptr(),
+                                    max_blocks_per_seq=self.plan.max_blocks,
+                                    num_kv_heads=c.hkv, head_dim=c.d, block_size=c.block,
+                                    kv_dtype=c.kv_dtype, layer=layer,
+                                    layer_stride=c.layer_stride(), stream=st)
+                assert rc == 0, f"append failed: {rc}"
+        torch.cuda.synchronize()
+
+    def launch(self, layer: int, stream: int, q_ptr=None, out_ptr=None) -> None:
+        c = self.cfg
+        rc = self.be.decode_v2(
+            output=out_ptr or self.out[layer].data_ptr(),
+            query=q_ptr or self.q[layer].data_ptr(),
+            block_tables=self.table.data_ptr(), seq_lens=self.seq_lens.data_ptr(),
+            num_seqs=self.B, num_heads=c.hq, num_kv_heads=c.hkv, head_dim=c.d,
+            max_blocks_per_seq=self.plan.max_blocks, block_size=c.block, kv_dtype=c.kv_dtype,
+            layer=layer, layer_stride=c.layer_stride(), scale=c.scale, split=1, stream=stream)
+        if rc != 0:
+            raise RuntimeError(f"decode launch failed: {rc}")
+
+    def step_bytes(self) -> int:
+        return wl.algorithmic_bytes(self.cfg, self.lens)
+
+    def host_sample(self, seqs_local: list[int], layer: int = 0):
+        """Copies the sampled requests' pages of one layer to a compact host
+        arena; returns (cfg1, lens, table rows over the host arena, arena)."""
+        import dataclasses
+        c = self.cfg
+        c1 = dataclasses.replace(c, layers=1, batch=len(seqs_local))
+        lens = self.lens[seqs_local]
+        plan_rows = self.plan.slots[seqs_local]
+        used = plan_rows[plan_rows >= 0]
+        host = np.zeros((len(used), c1.slot_bytes()), dtype=np.uint8)
+        slot_b = c.slot_bytes()
+        arena_view = self.arena.view(-1)
+        loff = layer * c.layer_stride()
+        remap = {}
+        for i, sl in enumerate(used):
+            a = int(sl) * slot_b + loff
+            host[i] = arena_view[a:a + c.layer_stride()].cpu().numpy()
+            remap[int(sl)] = i
+        slots = np.full(plan_rows.shape, -1, np.int64)
+        for r in range(plan_rows.shape[0]):
+            for b in range(plan_rows.shape[1]):
+                if plan_rows[r, b] >= 0:
+                    slots[r, b] = remap[int(plan_rows[r, b])]
+        plan = wl.PagePlan(seq_lens=lens, slots=slots, n_slots=len(used),
+                           max_blocks=plan_rows.shape[1], pages_used=len(used))
+        table = wl.block_table(plan, c1, host.ctypes.data)
+        return c1, lens, table, host
+
+
+def run_kllm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    os.environ["KLLM_GPU_DEVICE"] = str(local)
+    import kllm_b200 as kb
+    be = kb.Backend()
+    if be.backend != kb.KLLM_GPU_CUDA:
+        raise RuntimeError("libkllm_gpu: no sm_100 device")
+
+    cfg = wl.CONFIGS[args.config]
+    if args.layers:
+        cfg = __import__("dataclasses").replace(cfg, layers=args.layers)
+    lens_all = wl.context_lengths(cfg, args.seed)
+    shards = lpt_shard(lens_all, world)
+    mine = shards[rank]
+    rig = DecodeRig(cfg, mine, lens_all, be, torch, local, args.seed)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up
+    for _ in range(args.warmup):
+        for layer in range(cfg.layers):
+            rig.launch(layer, sp)
+    barrier()
+
+    # device-timed region: KV (63 GB at 1 GPU) is far larger than the 126 MB L2
+    clk = Clocks(local)
+    clk.start()
+    launches0 = be.stats().launches
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * cfg.layers + 1)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    k = 0
+    for _ in range(args.steps):
+        for layer in range(cfg.layers):
+            ev[k].record(stream)
+            rig.launch(layer, sp)
+            k += 1
+    ev[k].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = be.stats().launches - launches0
+    elapsed_ms = t0.elapsed_time(t1)
+    per_launch = [ev[i].elapsed_time(ev[i + 1]) for i in range(k)]
+
+    # end-to-end through the C ABI: pinned host Q in, bf16 O out, every step
+    host_q = torch.empty_like(rig.q, device="cpu").pin_memory()
+    host_q.copy_(rig.q.cpu())
+    host_o = torch.empty_like(rig.out, device="cpu").pin_memory()
+    host_lens = torch.from_numpy(rig.lens.copy()).pin_memory()
+    lib, ctx = be.lib, be.ctx
+    qb = rig.q[0].numel() * 2
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+
+    def e2e_step():
+        lib.kllm_gpu_memcpy_h2d_async(ctx, rig.seq_lens.data_ptr(), host_lens.data_ptr(),
+                                      host_lens.numel() * 4, sp)
+        for layer in range(cfg.layers):
+            lib.kllm_gpu_memcpy_h2d_async(ctx, rig.q[layer].data_ptr(),
+                                          host_q[layer].data_ptr(), qb, sp)
+            rig.launch(layer, sp)
+            lib.kllm_gpu_memcpy_d2h_async(ctx, host_o[layer].data_ptr(),
+                                          rig.out[layer].data_ptr(), qb, sp)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    my_bytes = rig.step_bytes()
+    stats = torch.tensor([elapsed_ms, e2e_ms, float(my_bytes), float(rig.B),
+                          float(np.mean(per_launch)), float(rig.arena_bytes)],
+                         dtype=torch.float64, device="cuda")
+    if world > 1:
+        gathered = [torch.zeros_like(stats) for _ in range(world)]
+        dist.all_gather(gathered, stats)
+        allst = torch.stack(gathered).cpu().numpy()
+    else:
+        allst = stats.cpu().numpy()[None]
+    t_ms = float(allst[:, 0].max())
+    te_ms = float(allst[:, 1].max())
+    total_bytes = float(allst[:, 2].sum())
+    total_tokens = float(allst[:, 3].sum())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_from_rig(rig, args)
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        peak, peak_kind = peaks()
+        ms_step = t_ms / args.steps
+        value = total_bytes * args.steps / (t_ms * 1e-3) / 1e9
+        e2e_val = total_bytes * args.steps / (te_ms * 1e-3) / 1e9
+        # roofline of the decode kernel: rank 0's algorithmic bytes per launch
+        # over its mean CUDA-event launch time (burst peak: timed per launch)
+        per_launch_bytes = float(allst[0, 2]) / cfg.layers
+        achieved = per_launch_bytes / (float(allst[0, 4]) * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded; KV quantized on device by the "
+                                     "append kernel)",
+            "config": {"workload": cfg.name, "batch": cfg.batch, "layers": cfg.layers,
+                       "hq": cfg.hq, "hkv": cfg.hkv, "head_dim": cfg.d, "block": cfg.block,
+                       "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)",
+                       "kv_gb_per_step": round(total_bytes / 1e9, 3),
+                       "arena_gb_rank0": round(float(allst[0, 5]) / 1e9, 2),
+                       "l2": "inputs larger than L2 (KV per step >> 126 MB)",
+                       "parallelism": f"request-sharded x{world} (LPT), no collective"},
+            "tokens_per_s": round(total_tokens * args.steps / (t_ms * 1e-3), 1),
+            "hbm_frac_8tbs": round(value / world / 8000.0, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "decode_kernel<128,1> (MX-FP8)"},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(cfg.layers * qb + rig.B * 4),
+                    "d2h_bytes_per_step": int(cfg.layers * qb)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline_from_rig(rig, args) -> dict:
+    """The reference CPU attention on a bounded sample of the GPU-resident
+    workload (one layer of a subset of requests, pages copied back), timed on
+    the host cores; also checks the GPU outputs of that sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    lib = oracle.ref()
+    kind, prefix = ("reference", "ref") if lib is not None else ("port", "orc")
+    if lib is None:
+        lib = oracle.orc()
+    order = np.argsort(rig.lens)
+    pick = sorted(int(i) for i in order[np.linspace(0, len(order) - 1, 24).astype(int)])
+    c1, lens, table, host = rig.host_sample(pick, layer=0)
+    q = rig.q[0][pick].contiguous().view(rig.torch.int16).cpu().numpy().view(np.uint16)
+    nthreads = os.cpu_count() or 1
+    out, wall, g, a = oracle.harness_decode(lib, prefix, q, table, lens, c1.hq, c1.hkv, c1.d,
+                                            table.shape[1], c1.scale, c1.block, c1.kv_dtype, 0,
+                                            nthreads)
+    reps, total = 1, wall
+    while total < args.cpu_seconds and reps < 200:
+        _, w2, _, _ = oracle.harness_decode(lib, prefix, q, table, lens, c1.hq, c1.hkv, c1.d,
+                                            table.shape[1], c1.scale, c1.block, c1.kv_dtype, 0,
+                                            nthreads)
+        total += w2
+        reps += 1
+    sample_bytes = wl.algorithmic_bytes(c1, lens, layers=1)
+    gpu = rig.out[0][pick].contiguous().view(rig.torch.int16).cpu().numpy().view(np.uint16)
+    gf, rf = wl.bf16_to_f32(gpu), wl.bf16_to_f32(out)
+    ok = bool(np.all(np.abs(gf - rf) <= 1e-3 + 2e-2 * np.abs(rf)))
+    return {"value": round(sample_bytes * reps / total / 1e9, 3), "unit": "GB/s",
+            "cores": nthreads, "kind": kind,
+            "sample": f"layer 0 of {len(pick)} requests ({int(lens.sum())} tokens, "
+                      f"{sample_bytes / 1e6:.1f} MB) x {reps} reps",
+            "gather_dequant_s": round(g, 4), "attention_s": round(a, 4),
+            "gpu_matches_reference_on_sample": ok}
+
+
+# ---------------------------------------------------------------------------
+# reference arm (CPU)
+# ---------------------------------------------------------------------------
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle
+    import kvcase
+    lib = oracle.ref()
+    kind, prefix = ("reference", "ref") if lib is not None else ("port", "orc")
+    if lib is None:
+        lib = oracle.orc()
+    cfg = wl.CONFIGS[args.config]
+    lens_all = wl.context_lengths(cfg, args.seed)
+    order = np.argsort(lens_all)
+    pick = sorted(int(i) for i in order[np.linspace(0, len(order) - 1, 24).astype(int)])
+    hc = kvcase.build_case(cfg, seq_lens=lens_all[pick], layers=1, tail_fill=0)
+    c = hc.cfg
+    nthreads = os.cpu_count() or 1
+    table = hc.host_table()
+    sample_bytes = wl.algorithmic_bytes(c, hc.seq_lens, layers=1)
+
+    def step():
+        return oracle.harness_decode(lib, prefix, hc.q[0], table, hc.seq_lens, c.hq, c.hkv,
+                                     c.d, hc.plan.max_blocks, c.scale, c.block, c.kv_dtype, 0,
+                                     nthreads)[1]
+    for _ in range(args.warmup):
+        step()
+    walls = [step() for _ in range(args.steps)]
+    t = sum(walls)
+    value = sample_bytes * args.steps / t / 1e9
+    full_step_s = (t / args.steps) * wl.algorithmic_bytes(cfg, lens_all) / sample_bytes
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "batch": cfg.batch, "layers": cfg.layers,
+                   "hq": cfg.hq, "hkv": cfg.hkv, "head_dim": cfg.d, "block": cfg.block,
+                   "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)"},
+        "tokens_per_s": round(cfg.batch / full_step_s, 2),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads,
+                         "kind": kind,
+                         "sample": f"layer 0 of {len(pick)} requests spanning the context "
+                                   f"range ({int(hc.seq_lens.sum())} tokens, "
+                                   f"{sample_bytes / 1e6:.1f} MB) per step"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
+    ap.add_argument("--config", default=wl.C3.name, choices=list(wl.CONFIGS))
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (smaller captures for profiling)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_kllm(args)
+
+
+if __name__ == "__main__":
+    main()

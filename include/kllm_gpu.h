@@ -1,0 +1,318 @@
+/* SPDX-License-Identifier: Apache-2.0 */
+/*
+ * kllm_gpu.h - C ABI of the B200 (sm_100a) paged-attention backend.
+ *
+ * Part 1 is the xpu-kllm GPU backend interface, kept symbol-for-symbol and
+ * signature-for-signature so existing callers (compute/infer_gpu.c) link
+ * against this library unchanged:
+ *     userspace/gpu/gpu_attention.h:19-24   enum kllm_gpu_backend
+ *     userspace/gpu/gpu_attention.h:26-38   struct kllm_gpu_attention_params
+ *     userspace/gpu/gpu_attention.h:43-62   create/destroy/get_backend/
+ *                                           paged_attention/malloc/free/
+ *                                           memcpy_h2d/get_stream
+ *     userspace/gpu/gpu_attention.h:70-73   kllm_gpu_paged_attention_cuda
+ *     userspace/gpu/paged_attention.cu:18-22 struct block_table_entry
+ *
+ * Part 2 adds versioned entry points the reference lacks: 16-token pages,
+ * the MX-FP8 KV format, split-KV partial outputs, KV append with
+ * quantize-on-write, the partial merge, chunked prefill, a bit-exact gather
+ * for tests and the NCCL split-KV exchange.
+ *
+ * Conventions (all calls):
+ *   - every pointer inside a params struct is a DEVICE pointer unless the
+ *     field comment says otherwise;
+ *   - `stream` is a cudaStream_t; NULL selects the context's own stream
+ *     (userspace/gpu/gpu_attention.c:82);
+ *   - launches are asynchronous; 0 means "launched", a negative value is one
+ *     of the KLLM_E* codes below and nothing was launched;
+ *   - no call allocates device memory except kllm_gpu_create and
+ *     kllm_gpu_malloc.
+ */
+#ifndef KLLM_GPU_H
+#define KLLM_GPU_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Part 1: reference interface (userspace/gpu/gpu_attention.h)              */
+/* ------------------------------------------------------------------------ */
+
+/* userspace/gpu/gpu_attention.h:19-24. This backend reports KLLM_GPU_CUDA on
+ * an sm_100 device and KLLM_GPU_NONE otherwise. */
+enum kllm_gpu_backend {
+	KLLM_GPU_NONE = 0,
+	KLLM_GPU_XE,
+	KLLM_GPU_CUDA,
+	KLLM_GPU_ROCM,
+};
+
+/* userspace/gpu/gpu_attention.h:26-38, unchanged. Semantics of the v1 call:
+ * BF16 Q/O [num_seqs][num_heads][head_dim]; BF16 K/V pages of 128 tokens laid
+ * out [num_kv_heads][128][head_dim] (userspace/gpu/paged_attention.cu:14,62-65);
+ * head_dim must be 64 or 128. */
+struct kllm_gpu_attention_params {
+	void *output;             /* device ptr: [num_seqs, num_heads, head_dim] bf16 */
+	const void *query;        /* device ptr */
+	const void *block_tables; /* device ptr: block_table_entry array */
+	const int *seq_lens;      /* device ptr */
+	int num_seqs;
+	int num_heads;
+	int num_kv_heads;
+	int head_dim;
+	int max_blocks_per_seq;
+	float scale;
+	void *stream;             /* cudaStream_t */
+};
+
+/* userspace/gpu/paged_attention.cu:18-22: one page descriptor, 24 bytes.
+ * An entry with valid == 0 or k_ptr == NULL is skipped, as in the reference
+ * kernel (paged_attention.cu:59-60). Page pointers must be 16-byte aligned. */
+struct kllm_block_table_entry {
+	void *k_ptr;
+	void *v_ptr;
+	int valid;
+};
+
+struct kllm_gpu_ctx;
+
+/* userspace/gpu/gpu_attention.h:43. Binds the device named by the env var
+ * KLLM_GPU_DEVICE (default: the current device), creates a non-blocking
+ * stream and a split-KV workspace. Returns a context whose backend is
+ * KLLM_GPU_NONE when no sm_100 device is usable; every compute call on such a
+ * context returns KLLM_ENODEV. Returns NULL only on host allocation failure. */
+struct kllm_gpu_ctx *kllm_gpu_create(void);
+/* userspace/gpu/gpu_attention.h:44 */
+void kllm_gpu_destroy(struct kllm_gpu_ctx *ctx);
+/* userspace/gpu/gpu_attention.h:47 */
+enum kllm_gpu_backend kllm_gpu_get_backend(struct kllm_gpu_ctx *ctx);
+/* userspace/gpu/gpu_attention.h:50-51. Same semantics as
+ * kllm_gpu_paged_attention_cuda, but uses the context's split-KV workspace,
+ * so long contexts are spread over every SM. */
+int kllm_gpu_paged_attention(struct kllm_gpu_ctx *ctx,
+			     const struct kllm_gpu_attention_params *params);
+/* userspace/gpu/gpu_attention.h:54-55 (the reference stubs return NULL). */
+void *kllm_gpu_malloc(struct kllm_gpu_ctx *ctx, uint64_t size);
+void kllm_gpu_free(struct kllm_gpu_ctx *ctx, void *ptr);
+/* userspace/gpu/gpu_attention.h:58-59: synchronous host-to-device copy
+ * (the reference stub returns -1). */
+int kllm_gpu_memcpy_h2d(struct kllm_gpu_ctx *ctx, void *dst,
+			const void *src, uint64_t size);
+/* userspace/gpu/gpu_attention.h:62: the context's cudaStream_t. */
+void *kllm_gpu_get_stream(struct kllm_gpu_ctx *ctx);
+
+/* userspace/gpu/gpu_attention.h:70-73 (defined at paged_attention.cu:121-146).
+ * Stateless launcher: needs no context and no workspace; every
+ * (seq, kv_head) pair is processed whole by one warp, as in the reference
+ * launch shape. Returns 0 when the launch was accepted, negative otherwise. */
+int kllm_gpu_paged_attention_cuda(
+    void *output, const void *query, const void *block_tables,
+    const int *seq_lens, int num_seqs, int num_heads, int num_kv_heads,
+    int head_dim, int max_blocks_per_seq, float scale, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Part 2: additions                                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Error codes (negative errno values). */
+#define KLLM_OK          0
+#define KLLM_EIO        (-5)    /* CUDA runtime / NCCL error */
+#define KLLM_ENOMEM     (-12)
+#define KLLM_ENODEV     (-19)   /* no usable sm_100 device */
+#define KLLM_EINVAL     (-22)   /* bad argument */
+#define KLLM_ENOSPC     (-28)   /* workspace too small */
+#define KLLM_ENOSYS     (-38)   /* shape not supported by this build */
+#define KLLM_ETIMEDOUT  (-110)  /* bounded host wait expired */
+
+/* Bits the kernels OR into *err_word (when given) instead of trapping. */
+#define KLLM_ERR_SEQ_TOO_LONG   0x1u  /* seq_len > max_blocks_per_seq * block_size: clamped */
+#define KLLM_ERR_MISALIGNED     0x2u  /* page pointer not 16-byte aligned: page skipped */
+#define KLLM_ERR_APPEND_NOPAGE  0x4u  /* append target page invalid / position out of table */
+
+/* KV page formats. One page holds `block_size` tokens of one layer.
+ *
+ * KLLM_KV_BF16: K page = [num_kv_heads][block_size][head_dim] bf16, V alike.
+ *
+ * KLLM_KV_MX_FP8_E4M3: K page = num_kv_heads head sections; each section is
+ *   [block_size][head_dim] E4M3 payload bytes followed by
+ *   [block_size][head_dim/8] E4M3 scale bytes (one scale per 8 consecutive
+ *   elements along head_dim, userspace/compute/mx_dequant.h:27). Real value =
+ *   e4m3(payload) * e4m3(scale), decoded as userspace/compute/mx_dequant.h:30-55
+ *   (0x7F/0xFF decode to +-480). V page alike.
+ *
+ * KLLM_KV_MX_BF16_COMPAT: the reference's own MX layout
+ *   (userspace/compute/mx_dequant.h:10-16): sections of [block_size][head_dim]
+ *   bf16 payload followed by [block_size][head_dim/8] scale bytes, written by
+ *   the reference quantizer mx_quant_to_bf16 (mx_dequant.h:105-136). Append
+ *   only (the reference never reads it on a GPU). */
+enum kllm_kv_dtype {
+	KLLM_KV_BF16 = 0,
+	KLLM_KV_MX_FP8_E4M3 = 1,
+	KLLM_KV_MX_BF16_COMPAT = 2,
+};
+
+/* Decode attention, versioned. Zero-initialise, set struct_size, fill in. */
+struct kllm_gpu_attention_params_v2 {
+	uint32_t struct_size;        /* sizeof(struct kllm_gpu_attention_params_v2) */
+	uint32_t flags;              /* reserved, 0 */
+	void *output;                /* bf16 [num_seqs][num_heads][head_dim]; may be NULL
+	                                when partial_m/l/o are given */
+	const void *query;           /* bf16 [num_seqs][num_heads][head_dim] */
+	const void *block_tables;    /* kllm_block_table_entry [num_seqs][max_blocks_per_seq] */
+	const int *seq_lens;         /* int32 [num_seqs]: tokens of context (<= 0: empty) */
+	int num_seqs;
+	int num_heads;               /* query heads */
+	int num_kv_heads;            /* num_heads % num_kv_heads == 0, ratio <= 8 */
+	int head_dim;                /* 64 or 128 */
+	int max_blocks_per_seq;
+	int block_size;              /* tokens per page: 16, 32, 64 or 128 */
+	int kv_dtype;                /* KLLM_KV_BF16 or KLLM_KV_MX_FP8_E4M3 */
+	int layer;                   /* page offset = layer * layer_stride bytes */
+	uint64_t layer_stride;       /* multiple of 16 */
+	float scale;                 /* softmax scale (1/sqrt(head_dim) typically) */
+	int split;                   /* 1 (default when 0): balance tiles over every SM with
+	                                split-KV; -1: one warp per (seq, kv_head), no workspace */
+	/* Optional split-KV triples, fp32, one per (seq, query head), for a
+	 * cross-GPU merge (kllm_gpu_merge_partials): m = max of scale*q.k (natural
+	 * log domain), l = sum exp(scale*q.k - m), o = normalised output
+	 * [num_seqs][num_heads][head_dim]. An empty context gives m = -inf, l = 0,
+	 * o = 0. All three or none. */
+	float *partial_m;
+	float *partial_l;
+	float *partial_o;
+	uint32_t *err_word;          /* optional; KLLM_ERR_* bits are OR-ed in */
+	void *workspace;             /* optional; NULL = the context's workspace */
+	uint64_t workspace_size;
+	void *stream;
+};
+
+int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
+				const struct kllm_gpu_attention_params_v2 *p);
+
+/* Bytes of workspace a split-KV decode needs on this context's device. */
+uint64_t kllm_gpu_decode_workspace_size(struct kllm_gpu_ctx *ctx, int num_seqs,
+					int num_kv_heads);
+
+/* KV append with quantize-on-write. Token i (row i of k/v) goes to position
+ * token_pos[i] of sequence token_seq[i]: page = block_tables[seq][pos /
+ * block_size], slot = pos % block_size. Rows whose page entry is invalid are
+ * skipped and flagged with KLLM_ERR_APPEND_NOPAGE.
+ *   BF16:            bytes copied.
+ *   MX_FP8_E4M3:     per 8 elements: amax; scale = smallest E4M3 >= amax/448
+ *                    (0 when amax == 0); payload = RNE-satfinite E4M3 of
+ *                    x / scale (0 when amax == 0).
+ *   MX_BF16_COMPAT:  mx_quant_to_bf16 (userspace/compute/mx_dequant.h:105-136),
+ *                    bit for bit, including its constant scale byte. */
+struct kllm_gpu_kv_append_params {
+	uint32_t struct_size;
+	uint32_t flags;
+	const void *k;               /* bf16 [num_tokens][num_kv_heads][head_dim] */
+	const void *v;               /* bf16 [num_tokens][num_kv_heads][head_dim] */
+	const int *token_seq;        /* int32 [num_tokens] */
+	const int *token_pos;        /* int32 [num_tokens] */
+	int num_tokens;
+	const void *block_tables;    /* kllm_block_table_entry [.][max_blocks_per_seq] */
+	int max_blocks_per_seq;
+	int num_kv_heads;
+	int head_dim;
+	int block_size;
+	int kv_dtype;
+	int layer;
+	uint64_t layer_stride;
+	uint32_t *err_word;
+	void *stream;
+};
+
+int kllm_gpu_kv_append_v2(struct kllm_gpu_ctx *ctx,
+			  const struct kllm_gpu_kv_append_params *p);
+
+/* Bit-exact logical view of the paged cache, for tests: for every
+ * (seq, kv_head) the valid tokens in order (invalid pages skipped, the last
+ * page cut at seq_len), dequantised to bf16 exactly (an E4M3 x E4M3 product
+ * is exact in bf16), written to k_out/v_out [num_seqs][num_kv_heads]
+ * [max_blocks_per_seq*block_size][head_dim]; counts_out [num_seqs]
+ * [num_kv_heads] receives the token counts. Rows past the count are zeroed. */
+struct kllm_gpu_gather_params {
+	uint32_t struct_size;
+	uint32_t flags;
+	void *k_out;
+	void *v_out;
+	int *counts_out;
+	const void *block_tables;
+	const int *seq_lens;
+	int num_seqs;
+	int num_kv_heads;
+	int head_dim;
+	int max_blocks_per_seq;
+	int block_size;
+	int kv_dtype;                /* KLLM_KV_BF16 or KLLM_KV_MX_FP8_E4M3 */
+	int layer;
+	uint64_t layer_stride;
+	void *stream;
+};
+
+int kllm_gpu_gather_debug(struct kllm_gpu_ctx *ctx,
+			  const struct kllm_gpu_gather_params *p);
+
+/* LSE merge of split-KV triples: for each of num_rows rows (seq x query
+ * head), M = max_i m_i, w_i = l_i exp(m_i - M), out = sum_i w_i o_i / sum_i w_i
+ * (0 when every l_i is 0). Inputs are stacked by part: m/l [num_parts]
+ * [num_rows], o [num_parts][num_rows][head_dim]. out: bf16 [num_rows]
+ * [head_dim]. */
+int kllm_gpu_merge_partials(struct kllm_gpu_ctx *ctx, const float *m,
+			    const float *l, const float *o, int num_parts,
+			    int num_rows, int head_dim, void *out, void *stream);
+
+/* Synchronous device-to-host copy (counterpart of kllm_gpu_memcpy_h2d). */
+int kllm_gpu_memcpy_d2h(struct kllm_gpu_ctx *ctx, void *dst,
+			const void *src, uint64_t size);
+/* Asynchronous copies on `stream` (NULL: the context stream). */
+int kllm_gpu_memcpy_h2d_async(struct kllm_gpu_ctx *ctx, void *dst,
+			      const void *src, uint64_t size, void *stream);
+int kllm_gpu_memcpy_d2h_async(struct kllm_gpu_ctx *ctx, void *dst,
+			      const void *src, uint64_t size, void *stream);
+/* Page-locked host memory for the async copies. */
+void *kllm_gpu_host_alloc(struct kllm_gpu_ctx *ctx, uint64_t size);
+void kllm_gpu_host_free(struct kllm_gpu_ctx *ctx, void *ptr);
+/* Waits for the context stream; returns KLLM_ETIMEDOUT after timeout_ms
+ * milliseconds (<= 0: wait without limit). */
+int kllm_gpu_synchronize(struct kllm_gpu_ctx *ctx, int timeout_ms);
+
+struct kllm_gpu_stats {
+	uint64_t launches;           /* kernels launched through this context */
+	uint64_t kv_bytes;           /* algorithmic KV bytes of decode launches
+	                                (valid pages x bytes per page, host estimate) */
+	uint64_t errors;             /* calls that returned an error */
+	int last_error;              /* last negative return code */
+	int device;                  /* CUDA ordinal */
+	int num_sms;
+};
+int kllm_gpu_get_stats(struct kllm_gpu_ctx *ctx, struct kllm_gpu_stats *out);
+
+/* Cross-GPU split-KV exchange over NCCL (NVLink). One context per rank.
+ * kllm_gpu_comm_get_unique_id runs on one rank; its 128 bytes reach the
+ * others through the caller's channel. Init is non-blocking and bounded:
+ * KLLM_ETIMEDOUT (communicator aborted) when the peers do not join within
+ * timeout_ms. */
+int kllm_gpu_comm_get_unique_id(uint8_t id[128]);
+int kllm_gpu_comm_init(struct kllm_gpu_ctx *ctx, int nranks, int rank,
+		       const uint8_t id[128], int timeout_ms);
+/* All-gathers this rank's triples (m, l [num_rows], o [num_rows][head_dim],
+ * fp32, as produced by kllm_gpu_paged_attention_v2's partial_* outputs) from
+ * every rank and merges them into out (bf16 [num_rows][head_dim]) on every
+ * rank. Enqueued on `stream`; the exchange is waited for with a bound of
+ * timeout_ms when timeout_ms > 0 (KLLM_ETIMEDOUT: communicator aborted). */
+int kllm_gpu_comm_merge(struct kllm_gpu_ctx *ctx, const float *m,
+			const float *l, const float *o, int num_rows,
+			int head_dim, void *out, void *stream, int timeout_ms);
+void kllm_gpu_comm_destroy(struct kllm_gpu_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLLM_GPU_H */

@@ -1,0 +1,235 @@
+# SPDX-License-Identifier: Apache-2.0
+"""GPU parity of the paged decode (through the C ABI) against the oracle.
+
+Tolerance (the parity contract for attention outputs): |gpu - oracle| <=
+1e-3 + 2e-2 |oracle| elementwise on the bf16 outputs.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import replace
+
+import numpy as np
+import pytest
+
+import kvcase
+from kllm_b200 import Backend, workloads as wl
+import kllm_b200 as kb
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def be():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    b = Backend()
+    assert b.backend == kb.KLLM_GPU_CUDA, "libkllm_gpu found no sm_100 device"
+    yield b
+    b.close()
+
+
+def run_v2(be, dc, **over):
+    import torch
+    kw = dc.decode_kwargs(**over)
+    kw.setdefault("stream", torch.cuda.current_stream().cuda_stream)
+    rc = be.decode_v2(**kw)
+    assert rc == 0, f"kllm_gpu_paged_attention_v2 returned {rc}"
+    return dc.out_host()
+
+
+@pytest.mark.parametrize("split", [1, -1])
+def test_c1_bf16(be, split):
+    hc = kvcase.build_case(wl.C1)
+    dc = kvcase.DeviceCase(hc)
+    got = run_v2(be, dc, split=split)
+    kvcase.assert_close_bf16(got, hc.oracle_decode(), what=f"C1 split={split}")
+
+
+def test_c2_mx_fp8(be):
+    hc = kvcase.build_case(wl.C2, batch=16)
+    dc = kvcase.DeviceCase(hc)
+    got = run_v2(be, dc)
+    kvcase.assert_close_bf16(got, hc.oracle_decode(), what="C2 mx")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+@pytest.mark.parametrize("block", [32, 64, 128])
+def test_block_sizes(be, kv, block):
+    cfg = replace(wl.C1, block=block, kv_dtype=kv, arena_slots=None,
+                  mult_lo=0.5 if kv else None, mult_hi=4.0 if kv else None)
+    hc = kvcase.build_case(cfg, seq_lens=[1, 15, 16, 17, 200, 511, 64, 129])
+    dc = kvcase.DeviceCase(hc)
+    kvcase.assert_close_bf16(run_v2(be, dc), hc.oracle_decode(), what=f"bs={block} kv={kv}")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (32, 8), (64, 8), (12, 4)])
+def test_gqa_groups(be, kv, hq, hkv):
+    cfg = replace(wl.C1, hq=hq, hkv=hkv, kv_dtype=kv, arena_slots=None)
+    hc = kvcase.build_case(cfg, seq_lens=[70, 300, 1, 33])
+    dc = kvcase.DeviceCase(hc)
+    kvcase.assert_close_bf16(run_v2(be, dc), hc.oracle_decode(), what=f"G={hq // hkv}")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+def test_head_dim_64(be, kv):
+    cfg = replace(wl.C1, d=64, hq=16, hkv=4, kv_dtype=kv, arena_slots=None)
+    hc = kvcase.build_case(cfg, seq_lens=[4, 100, 257, 16, 0])
+    dc = kvcase.DeviceCase(hc)
+    kvcase.assert_close_bf16(run_v2(be, dc), hc.oracle_decode(), what="d=64")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+def test_edges_empty_invalid_ragged(be, kv):
+    """Empty contexts (0 and negative), single tokens, skipped (invalid) pages
+    including a skipped last page and a fully skipped sequence."""
+    cfg = replace(wl.C1, kv_dtype=kv, arena_slots=None)
+    lens = [0, 1, 17, 48, 160, 0, 33, 5, -3, 400]
+    invalid = [(2, 0), (3, 2), (4, 3), (4, 4), (6, 2), (7, 0), (9, 10)]
+    hc = kvcase.build_case(cfg, seq_lens=lens, invalid=invalid)
+    dc = kvcase.DeviceCase(hc)
+    dc.out.fill_(0x3F80)  # must be overwritten, zeros included
+    got = run_v2(be, dc)
+    ref = hc.oracle_decode()
+    kvcase.assert_close_bf16(got, ref, what="edges")
+    for s in (0, 5, 7, 8):
+        assert not got[s].any(), f"seq {s} should be all zeros"
+
+
+def test_split_equals_whole_long(be):
+    """One long context split over every SM vs one warp per segment."""
+    cfg = replace(wl.C4, batch=1, ctx_lo=20000, ctx_hi=20000, hq=32)
+    hc = kvcase.build_case(cfg)
+    dc = kvcase.DeviceCase(hc)
+    a = run_v2(be, dc, split=1)
+    b = run_v2(be, dc, split=-1)
+    ref = hc.oracle_decode()
+    kvcase.assert_close_bf16(a, ref, what="split")
+    kvcase.assert_close_bf16(b, ref, what="whole")
+
+
+def test_repeat_calls_counters_reset(be):
+    """The split-KV arrival counters must be back at zero after each call."""
+    hc = kvcase.build_case(wl.C2, batch=4)
+    dc = kvcase.DeviceCase(hc)
+    ref = hc.oracle_decode()
+    first = run_v2(be, dc)
+    for _ in range(3):
+        assert np.array_equal(run_v2(be, dc), first)
+    kvcase.assert_close_bf16(first, ref, what="repeat")
+
+
+def test_partials_and_merge(be):
+    """partial_m/l/o against the oracle triples; the merge of two halves of a
+    context equals the whole-context decode (split-KV across GPUs, on one)."""
+    import torch
+    cfg = replace(wl.C2, batch=3)
+    hc = kvcase.build_case(cfg, seq_lens=[3000, 1, 0])
+    dc = kvcase.DeviceCase(hc)
+    S, Hq, D = 3, cfg.hq, cfg.d
+    pm = torch.empty((S, Hq), dtype=torch.float32, device="cuda")
+    pl = torch.empty_like(pm)
+    po = torch.empty((S, Hq, D), dtype=torch.float32, device="cuda")
+    rc = be.decode_v2(**dc.decode_kwargs(output=None, partial_m=pm.data_ptr(),
+                                         partial_l=pl.data_ptr(), partial_o=po.data_ptr()))
+    assert rc == 0
+    torch.cuda.synchronize()
+    m, l, o = hc.oracle_partials()
+    kvcase.assert_close_f32(pm.cpu().numpy(), m, atol=2e-3, rtol=1e-3, what="m")
+    kvcase.assert_close_f32(pl.cpu().numpy(), l, atol=1e-2, rtol=1e-2, what="l")
+    kvcase.assert_close_f32(po.cpu().numpy(), o, what="o")
+
+    # two "ranks": first and second half of every block table
+    mb = hc.plan.max_blocks
+    half = mb // 2
+    lens = hc.seq_lens
+    t_all = wl.block_table(hc.plan, cfg, dc.arena.data_ptr(), hc.valid)
+    parts = []
+    for r in range(2):
+        t = np.zeros_like(t_all)
+        lo, hi = (0, half) if r == 0 else (half, mb)
+        t[:, : hi - lo] = t_all[:, lo:hi]
+        l_r = np.clip(lens - lo * cfg.block, 0, (hi - lo) * cfg.block).astype(np.int32)
+        tt = torch.from_numpy(t.view(np.uint8).copy()).cuda()
+        ll = torch.from_numpy(l_r).cuda()
+        m_r = torch.empty((S, Hq), dtype=torch.float32, device="cuda")
+        l_rr = torch.empty_like(m_r)
+        o_r = torch.empty((S, Hq, D), dtype=torch.float32, device="cuda")
+        rc = be.decode_v2(**dc.decode_kwargs(output=None, block_tables=tt.data_ptr(),
+                                             seq_lens=ll.data_ptr(), max_blocks_per_seq=mb,
+                                             partial_m=m_r.data_ptr(), partial_l=l_rr.data_ptr(),
+                                             partial_o=o_r.data_ptr()))
+        assert rc == 0
+        parts.append((m_r, l_rr, o_r, tt, ll))
+    M = torch.stack([p[0] for p in parts]).contiguous()
+    L = torch.stack([p[1] for p in parts]).contiguous()
+    O = torch.stack([p[2] for p in parts]).contiguous()
+    out = torch.zeros((S * Hq, D), dtype=torch.int16, device="cuda")
+    rc = be.merge(M.data_ptr(), L.data_ptr(), O.data_ptr(), 2, S * Hq, D, out.data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    merged = out.cpu().numpy().view(np.uint16).reshape(S, Hq, D)
+    kvcase.assert_close_bf16(merged, hc.oracle_decode(), what="merge of halves")
+
+
+def test_v1_entry_points(be):
+    """kllm_gpu_paged_attention (ctx) and kllm_gpu_paged_attention_cuda
+    (stateless) with the v1 contract: BF16 pages of 128 tokens."""
+    import torch
+    cfg = replace(wl.C1, block=128, arena_slots=None)
+    hc = kvcase.build_case(cfg, seq_lens=[1, 127, 128, 129, 700, 0, 1000, 300])
+    dc = kvcase.DeviceCase(hc)
+    ref = hc.oracle_decode()
+    st = torch.cuda.current_stream().cuda_stream
+    rc = be.decode_v1(output=dc.out.data_ptr(), query=dc.q[0].data_ptr(),
+                      block_tables=dc.table.data_ptr(), seq_lens=dc.seq_lens.data_ptr(),
+                      num_seqs=cfg.batch, num_heads=cfg.hq, num_kv_heads=cfg.hkv,
+                      head_dim=cfg.d, max_blocks_per_seq=hc.plan.max_blocks, scale=cfg.scale,
+                      stream=st)
+    assert rc == 0
+    kvcase.assert_close_bf16(dc.out_host(), ref, what="v1 ctx")
+    dc.out.zero_()
+    rc = be.lib.kllm_gpu_paged_attention_cuda(
+        dc.out.data_ptr(), dc.q[0].data_ptr(), dc.table.data_ptr(), dc.seq_lens.data_ptr(),
+        cfg.batch, cfg.hq, cfg.hkv, cfg.d, hc.plan.max_blocks, ctypes.c_float(cfg.scale), st)
+    assert rc == 0
+    kvcase.assert_close_bf16(dc.out_host(), ref, what="v1 stateless")
+
+
+def test_layers_and_golden_c1(be):
+    """Multi-layer pages (layer stride) for layer 1, and C1 against the
+    golden output computed by the reference's own code."""
+    import golden
+    cfg = replace(wl.C2, batch=4, layers=2)
+    hc = kvcase.build_case(cfg)
+    dc = kvcase.DeviceCase(hc)
+    got = run_v2(be, dc, layer=1)
+    kvcase.assert_close_bf16(got, hc.oracle_decode(layer=1), what="layer 1")
+
+    hc1 = kvcase.build_case(wl.C1)
+    dc1 = kvcase.DeviceCase(hc1)
+    kvcase.assert_close_bf16(run_v2(be, dc1), golden.load()["c1_out"], what="C1 golden")
+
+
+def test_seq_too_long_flag_and_clamp(be):
+    import torch
+    cfg = replace(wl.C1, arena_slots=None)
+    hc = kvcase.build_case(cfg, seq_lens=[64, 64])
+    dc = kvcase.DeviceCase(hc)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dc.seq_lens.copy_(torch.tensor([64, 999], dtype=torch.int32))
+    got = run_v2(be, dc, err_word=err.data_ptr())
+    assert int(err.item()) & kb.ERR_SEQ_TOO_LONG
+    kvcase.assert_close_bf16(got, hc.oracle_decode(), what="clamped")
+
+
+def test_rejects_bad_shapes(be):
+    hc = kvcase.build_case(wl.C1, batch=2)
+    dc = kvcase.DeviceCase(hc)
+    assert be.decode_v2(**dc.decode_kwargs(head_dim=96)) == kb.ENOSYS
+    assert be.decode_v2(**dc.decode_kwargs(num_heads=30)) == kb.EINVAL
+    assert be.decode_v2(**dc.decode_kwargs(block_size=24)) == kb.ENOSYS
+    assert be.decode_v2(**dc.decode_kwargs(kv_dtype=7)) == kb.ENOSYS
+    assert be.decode_v2(**dc.decode_kwargs(layer_stride=8, layer=1)) == kb.EINVAL

@@ -1,0 +1,83 @@
+/* SPDX-License-Identifier: Apache-2.0 */
+/*
+ * kllm_internal.h - launch interface between the C host shim (kllm_shim.c)
+ * and the CUDA translation units. Plain C, no CUDA types.
+ */
+#ifndef KLLM_INTERNAL_H
+#define KLLM_INTERNAL_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KLLM_DEC_WARPS      4     /* warps per decode CTA */
+#define KLLM_MAX_GROUP      8     /* query heads per kv head (mma N) */
+#define KLLM_SLOT_FLOATS    1040  /* one split-KV partial: o[8][128], m[8], l[8] */
+#define KLLM_MAX_SEQS_LAUNCH 4096 /* sequences per decode launch (smem prefix) */
+
+#define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
+
+struct kllm_decode_args {
+	void *out;                /* bf16 [S][Hq][D] or NULL */
+	const void *q;            /* bf16 [S][Hq][D] */
+	const void *table;        /* 24-byte entries [S][max_blocks] */
+	const int *seq_lens;      /* [S] */
+	int num_seqs;
+	int num_heads;
+	int num_kv_heads;
+	int group;                /* num_heads / num_kv_heads */
+	int head_dim;             /* 64 or 128 */
+	int max_blocks;
+	int block_size;           /* 16..128, multiple of 16 */
+	int kv_dtype;             /* 0 bf16, 1 mx-fp8 */
+	uint64_t layer_off;       /* bytes added to k_ptr/v_ptr */
+	float scale_log2;         /* softmax scale * log2(e) */
+	float *pm, *pl, *po;      /* optional split-KV triples */
+	uint32_t *err;            /* optional error word */
+	int split;                /* 1: tile-balanced split-KV; 0: one warp per segment */
+	float *ws_part;           /* split: partial slots [warps][2][KLLM_SLOT_FLOATS] */
+	unsigned *ws_cnt;         /* split: arrival counters [S*Hkv], zero between calls */
+	int total_warps;          /* warps launched (grid * KLLM_DEC_WARPS) */
+};
+
+/* Dynamic shared memory of one decode CTA for this shape. */
+size_t kllm_decode_smem_bytes(int head_dim, int kv_dtype, int num_seqs);
+/* Resident CTAs per SM for this shape (0 on error). */
+int kllm_decode_ctas_per_sm(int head_dim, int kv_dtype, int num_seqs);
+/* Launches the decode on `stream` with `grid` CTAs; 0 or a cudaError_t. */
+int kllm_decode_launch(const struct kllm_decode_args *a, int grid,
+		       void *stream);
+
+struct kllm_append_args {
+	const void *k, *v;
+	const int *token_seq, *token_pos;
+	int num_tokens;
+	const void *table;
+	int max_blocks, num_kv_heads, head_dim, block_size, kv_dtype;
+	uint64_t layer_off;
+	uint32_t *err;
+};
+int kllm_append_launch(const struct kllm_append_args *a, void *stream);
+
+struct kllm_gather_args {
+	void *k_out, *v_out;
+	int *counts;
+	const void *table;
+	const int *seq_lens;
+	int num_seqs, num_kv_heads, head_dim, max_blocks, block_size, kv_dtype;
+	uint64_t layer_off;
+};
+int kllm_gather_launch(const struct kllm_gather_args *a, void *stream);
+
+int kllm_merge_launch(const float *m, const float *l, const float *o,
+		      int num_parts, int num_rows, int head_dim, void *out,
+		      void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLLM_INTERNAL_H */

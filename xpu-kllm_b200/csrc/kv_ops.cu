@@ -1,0 +1,292 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// kv_ops.cu - the paged-cache side of the hot path on sm_100a:
+//   * KV append with quantize-on-write (MX-FP8, the reference's BF16-payload
+//     MX layout, or plain BF16);
+//   * the bit-exact gather used by tests to read the cache back;
+//   * the log-sum-exp merge of split-KV partial triples (cross-GPU split).
+
+#include "kllm_device.cuh"
+#include "kllm_internal.h"
+
+#include <math_constants.h>
+
+namespace kllm {
+namespace {
+
+struct DevEntry {  // userspace/gpu/paged_attention.cu:18-22
+	unsigned long long k, v;
+	int valid;
+	int pad;
+};
+
+__device__ __forceinline__ size_t section_bytes(int kv_dtype, int bs, int d)
+{
+	if (kv_dtype == 1)
+		return (size_t)bs * d + (size_t)bs * (d / 8);
+	if (kv_dtype == 2)
+		return (size_t)bs * d * 2 + (size_t)bs * (d / 8);
+	return (size_t)bs * d * 2;
+}
+
+// E4M3 code -> float, the reference decoder's values
+// (userspace/compute/mx_dequant.h:30-55; 0x7F -> 480).
+__device__ __forceinline__ float e4m3_value(uint32_t code)
+{
+	const uint32_t e = (code >> 3) & 0xFu, m = code & 0x7u;
+	float v;
+	if (e != 0)
+		v = __uint_as_float(((e + 120u) << 23) | (m << 20));
+	else
+		v = (float)m * 0.001953125f;  // m * 2^-9
+	return (code & 0x80u) ? -v : v;
+}
+
+// Two floats -> two E4M3 codes, round to nearest even, saturate to +-448.
+// Returns lo in byte 0 and hi in byte 1.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi)
+{
+	uint16_t r;
+	asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+	return r;
+}
+
+// Smallest E4M3 code >= amax / 448 (the reference quantizer's scale rule,
+// mx_dequant.h:119-120, with a real E4M3 encoding in place of its stub).
+__device__ __forceinline__ uint32_t mx_scale_code(float amax)
+{
+	if (!(amax > 0.f))
+		return 0u;
+	const float t = __fdiv_rn(amax, 448.0f);
+	if (t > 448.0f)
+		return 0x7Eu;
+	uint32_t c = cvt_e4m3x2(t, 0.f) & 0xFFu;
+	if (e4m3_value(c) < t)
+		++c;
+	return c == 0u ? 1u : c;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// One thread = one 8-element micro-block of one (token, K|V, kv head) row.
+__global__ void append_kernel(const kllm_append_args a)
+{
+	const int nb = a.head_dim / 8;
+	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
+	if (t >= total)
+		return;
+	const int b = (int)(t % nb);
+	const long long r = t / nb;
+	const int h = (int)(r % a.num_kv_heads);
+	const int kv = (int)((r / a.num_kv_heads) % 2);
+	const int i = (int)(r / (2LL * a.num_kv_heads));
+
+	const int seq = a.token_seq[i], pos = a.token_pos[i];
+	const int blk = pos >= 0 ? pos / a.block_size : -1;
+	if (seq < 0 || blk < 0 || blk >= a.max_blocks) {
+		if (a.err && b == 0)
+			atomicOr(a.err, 0x4u);
+		return;
+	}
+	const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+			    (size_t)seq * a.max_blocks + blk;
+	const unsigned long long base = kv ? e->v : e->k;
+	if (!e->valid || !e->k || !base) {
+		if (a.err && b == 0)
+			atomicOr(a.err, 0x4u);
+		return;
+	}
+	const int slot = pos - blk * a.block_size;
+	const int d = a.head_dim, bs = a.block_size;
+	uint8_t *sec = reinterpret_cast<uint8_t *>(base) + a.layer_off +
+		       (size_t)h * section_bytes(a.kv_dtype, bs, d);
+	const uint4 x = *reinterpret_cast<const uint4 *>(
+	    reinterpret_cast<const uint8_t *>(kv ? a.v : a.k) +
+	    (((size_t)i * a.num_kv_heads + h) * d + (size_t)b * 8) * 2);
+
+	if (a.kv_dtype == 0) {
+		*reinterpret_cast<uint4 *>(sec + ((size_t)slot * d + b * 8) * 2) = x;
+		return;
+	}
+	float f[8] = {bf16lo(x.x), bf16hi(x.x), bf16lo(x.y), bf16hi(x.y),
+		      bf16lo(x.z), bf16hi(x.z), bf16lo(x.w), bf16hi(x.w)};
+	float amax = 0.f;
+#pragma unroll
+	for (int k = 0; k < 8; ++k)
+		amax = fmaxf(amax, fabsf(f[k]));
+
+	if (a.kv_dtype == 1) {
+		const uint32_t code = mx_scale_code(amax);
+		uint32_t lo = 0u, hi = 0u;
+		if (code != 0u) {
+			const float s = e4m3_value(code);
+			uint32_t p[4];
+#pragma unroll
+			for (int k = 0; k < 4; ++k)
+				p[k] = cvt_e4m3x2(__fdiv_rn(f[2 * k], s),
+						  __fdiv_rn(f[2 * k + 1], s));
+			lo = p[0] | (p[1] << 16);
+			hi = p[2] | (p[3] << 16);
+		}
+		*reinterpret_cast<uint2 *>(sec + (size_t)slot * d + b * 8) = make_uint2(lo, hi);
+		sec[(size_t)bs * d + (size_t)slot * (d / 8) + b] = (uint8_t)code;
+		return;
+	}
+
+	// kv_dtype 2: mx_quant_to_bf16 (userspace/compute/mx_dequant.h:105-136)
+	const float scale = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+	const float inv = __fdiv_rn(1.0f, scale);
+	uint32_t outw[4];
+#pragma unroll
+	for (int k = 0; k < 4; ++k) {
+		uint32_t pr = 0;
+#pragma unroll
+		for (int hlf = 0; hlf < 2; ++hlf) {
+			uint32_t bits = __float_as_uint(__fmul_rn(f[2 * k + hlf], inv));
+			bits += 0x7FFFu + ((bits >> 16) & 1u);
+			pr |= (bits >> 16) << (16 * hlf);
+		}
+		outw[k] = pr;
+	}
+	*reinterpret_cast<uint4 *>(sec + ((size_t)slot * d + b * 8) * 2) =
+	    make_uint4(outw[0], outw[1], outw[2], outw[3]);
+	sec[(size_t)bs * d * 2 + (size_t)slot * (d / 8) + b] = amax > 0.f ? 64 : 0;
+}
+
+// One warp per (seq, kv head): walk the pages in order, skip invalid
+// entries, dequantise every valid token row exactly to bf16.
+__global__ void gather_kernel(const kllm_gather_args a)
+{
+	__shared__ uint32_t lut[256];
+	for (int i = threadIdx.x; i < 256; i += blockDim.x)
+		lut[i] = mx_scale_lut_entry((uint32_t)i);
+	__syncthreads();
+
+	const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	const int lane = threadIdx.x & 31;
+	if (warp >= a.num_seqs * a.num_kv_heads)
+		return;
+	const int s = warp / a.num_kv_heads, h = warp % a.num_kv_heads;
+	const int d = a.head_dim, bs = a.block_size;
+	const size_t cap = (size_t)a.max_blocks * bs;
+	uint16_t *ko = reinterpret_cast<uint16_t *>(a.k_out) +
+		       ((size_t)s * a.num_kv_heads + h) * cap * d;
+	uint16_t *vo = reinterpret_cast<uint16_t *>(a.v_out) +
+		       ((size_t)s * a.num_kv_heads + h) * cap * d;
+	int len = a.seq_lens[s];
+	len = len < 0 ? 0 : len;
+	if (len > (int)cap)
+		len = (int)cap;
+	const int nblocks = (len + bs - 1) / bs;
+	const size_t sec = section_bytes(a.kv_dtype, bs, d);
+	size_t n = 0;
+	for (int blk = 0; blk < nblocks; ++blk) {
+		const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+				    (size_t)s * a.max_blocks + blk;
+		if (!e->valid || !e->k)
+			continue;
+		const int ntok = min(bs, len - blk * bs);
+		for (int kv = 0; kv < 2; ++kv) {
+			const uint8_t *secp = reinterpret_cast<const uint8_t *>(kv ? e->v : e->k) +
+					      a.layer_off + (size_t)h * sec;
+			uint16_t *dst = (kv ? vo : ko) + n * d;
+			for (int idx = lane; idx < ntok * d; idx += 32) {
+				const int t = idx / d, col = idx - t * d;
+				uint16_t val;
+				if (a.kv_dtype == 1) {
+					const uint32_t pbyte = secp[(size_t)t * d + col];
+					const uint32_t sbyte = secp[(size_t)bs * d + (size_t)t * (d / 8) + col / 8];
+					uint32_t x = bf16x2_mul(e4m3x2_to_bf16x2_raw(pbyte, false), lut[sbyte]);
+					x = bf16x2_mul(x, 0x43804380u);  // * 256, exact
+					val = (uint16_t)(x & 0xFFFFu);
+				} else {
+					val = reinterpret_cast<const uint16_t *>(secp)[(size_t)t * d + col];
+				}
+				dst[(size_t)t * d + col] = val;
+			}
+		}
+		n += ntok;
+	}
+	for (size_t idx = n * d + lane; idx < cap * d; idx += 32) {
+		ko[idx] = 0;
+		vo[idx] = 0;
+	}
+	if (lane == 0)
+		a.counts[(size_t)s * a.num_kv_heads + h] = (int)n;
+}
+
+// One warp per row: M = max m_p, w_p = l_p exp(m_p - M), out = sum w_p o_p / sum w_p.
+__global__ void merge_kernel(const float *m, const float *l, const float *o,
+			     int parts, int rows, int d, uint16_t *out)
+{
+	const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	const int lane = threadIdx.x & 31;
+	if (row >= rows)
+		return;
+	float M = -CUDART_INF_F;
+	for (int p = 0; p < parts; ++p) {
+		const float lp = l[(size_t)p * rows + row];
+		if (lp > 0.f)
+			M = fmaxf(M, m[(size_t)p * rows + row]);
+	}
+	float wsum = 0.f;
+	for (int p = 0; p < parts; ++p) {
+		const float lp = l[(size_t)p * rows + row];
+		if (lp > 0.f)
+			wsum += lp * expf(m[(size_t)p * rows + row] - M);
+	}
+	const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+	for (int col = lane; col < d; col += 32) {
+		float acc = 0.f;
+		for (int p = 0; p < parts; ++p) {
+			const float lp = l[(size_t)p * rows + row];
+			if (lp > 0.f)
+				acc += lp * expf(m[(size_t)p * rows + row] - M) *
+				       o[((size_t)p * rows + row) * d + col];
+		}
+		__nv_bfloat16 b = __float2bfloat16_rn(acc * inv);
+		out[(size_t)row * d + col] = *reinterpret_cast<uint16_t *>(&b);
+	}
+}
+
+}  // namespace
+}  // namespace kllm
+
+using namespace kllm;
+
+extern "C" int kllm_append_launch(const struct kllm_append_args *a, void *stream)
+{
+	const long long total = (long long)a->num_tokens * 2 * a->num_kv_heads * (a->head_dim / 8);
+	if (total <= 0)
+		return 0;
+	const int threads = 256;
+	const long long blocks = (total + threads - 1) / threads;
+	append_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+	return (int)cudaGetLastError();
+}
+
+extern "C" int kllm_gather_launch(const struct kllm_gather_args *a, void *stream)
+{
+	const int warps = a->num_seqs * a->num_kv_heads;
+	if (warps <= 0)
+		return 0;
+	const int threads = 128;
+	const int blocks = (warps * 32 + threads - 1) / threads;
+	gather_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+	return (int)cudaGetLastError();
+}
+
+extern "C" int kllm_merge_launch(const float *m, const float *l, const float *o,
+				 int num_parts, int num_rows, int head_dim,
+				 void *out, void *stream)
+{
+	if (num_rows <= 0)
+		return 0;
+	const int threads = 128;
+	const int blocks = (num_rows * 32 + threads - 1) / threads;
+	merge_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+	    m, l, o, num_parts, num_rows, head_dim, static_cast<uint16_t *>(out));
+	return (int)cudaGetLastError();
+}

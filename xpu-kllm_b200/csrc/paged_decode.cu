@@ -1,0 +1,831 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// paged_decode.cu - GQA paged-attention decode for sm_100a.
+//
+// Replaces paged_attention_kernel_cuda (userspace/gpu/paged_attention.cu:24-119):
+// the same block-table gather (entries {k_ptr, v_ptr, valid}, invalid entries
+// skipped, last page cut at seq_len: paged_attention.cu:55-68), the same GQA
+// map (kv_head = q_head / (Hq/Hkv): paged_attention.cu:45), online softmax
+// (paged_attention.cu:86-98, with every output lane rescaled) and a BF16 RNE
+// store (paged_attention.cu:109-118). Empty contexts give zeros
+// (paged_attention.cu:110 with exp_sum == 0).
+//
+// Work decomposition. A "segment" is one (seq, kv_head) pair; its context is
+// cut into tiles of 16 tokens. All tiles of a launch are laid end to end
+// (seq-major, then kv head, then tile) and every warp of a persistent grid
+// takes an equal contiguous range of that list, so the HBM stream is
+// balanced to within one tile no matter how ragged the context lengths are.
+// A segment covered by several warps produces fp32 partials (m, l, o) in the
+// workspace; the last warp to finish it (arrival counter) merges them with
+// the log-sum-exp rule. Without a workspace, warps take whole segments.
+//
+// Per warp, per tile: lane 0 streams the tile's K and V (and, for MX, their
+// scale bytes) from the page into a private shared-memory ring with
+// cp.async.bulk (TMA engine, mbarrier completion, L2 evict-first), several
+// tiles ahead; block-table entries are prefetched 32 tiles ahead by the whole
+// warp. The G query heads of the segment share every K/V byte:
+//   S^T[16 tok x 8 heads] = K_tile[16 x D] . Q^T   (mma.m16n8k16, bf16)
+//   P^T -> bf16, transposed in registers (movmatrix)
+//   O^T[D x 8 heads] += V_tile^T[D x 16] . P^T     (mma.m16n8k16, bf16)
+// MX-FP8 tiles are dequantised in registers to bf16 exactly (see
+// kllm_device.cuh). Dimensions are permuted consistently inside each
+// contraction so that every lane reads contiguous 16-byte runs of shared
+// memory; the output permutation is undone at the store.
+
+#include "kllm_device.cuh"
+#include "kllm_internal.h"
+
+#include <math_constants.h>
+
+namespace kllm {
+namespace {
+
+constexpr int kTile = 16;
+constexpr int kWarps = KLLM_DEC_WARPS;
+constexpr int kSlotO = 0;                       // o[8][128]
+constexpr int kSlotM = KLLM_MAX_GROUP * 128;    // m[8]
+constexpr int kSlotL = kSlotM + KLLM_MAX_GROUP; // l[8]
+
+template <int D, int KVT>
+struct Geom {
+	static constexpr bool MX = (KVT == 1);
+	static constexpr int PAY = MX ? kTile * D : kTile * D * 2;  // payload / tile
+	static constexpr int SCL = MX ? kTile * D / 8 : 0;          // scales / tile
+	static constexpr int KV = PAY + SCL;                        // one of K, V
+	static constexpr int STAGE = 2 * KV;
+	static constexpr int NST = MX ? 4 : 3;                      // ring depth
+};
+
+struct DevEntry {  // userspace/gpu/paged_attention.cu:18-22 (24 bytes)
+	unsigned long long k, v;
+	int valid;
+	int pad;
+};
+
+struct Seg {
+	int s, h, j, ts;  // seq, kv head, tile in segment, tiles in segment
+};
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a)
+{
+	return (x + a - 1) / a * a;
+}
+
+struct SmemLayout {
+	size_t stage, bar, meta, lut, prefix, slen, total;
+	__host__ __device__ SmemLayout(int stage_bytes, int nst, int S)
+	{
+		stage = 0;
+		bar = align_up((size_t)stage_bytes * nst * kWarps, 128);
+		meta = bar + sizeof(uint64_t) * nst * kWarps;
+		lut = align_up(meta + sizeof(int) * nst * kWarps, 16);
+		prefix = lut + 256 * sizeof(uint32_t);
+		slen = prefix + sizeof(int) * (S + 1);
+		total = slen + sizeof(int) * S;
+	}
+};
+
+// Largest s in [0,S) with prefix[s]*H <= x (x < prefix[S]*H): the segment
+// holding flattened tile x. Sequences without tiles are never returned.
+__device__ __forceinline__ Seg locate(const int *prefix, int S, int H,
+				       long long x)
+{
+	int lo = 0, hi = S - 1;
+	while (lo < hi) {
+		int mid = (lo + hi + 1) >> 1;
+		if ((long long)prefix[mid] * H <= x)
+			lo = mid;
+		else
+			hi = mid - 1;
+	}
+	Seg c;
+	c.s = lo;
+	c.ts = prefix[lo + 1] - prefix[lo];
+	long long rel = x - (long long)prefix[lo] * H;
+	c.h = (int)(rel / c.ts);
+	c.j = (int)(rel - (long long)c.h * c.ts);
+	return c;
+}
+
+__device__ __forceinline__ long long seg_start_at_or_after(
+    const int *prefix, int S, int H, long long T, long long y)
+{
+	if (y >= T)
+		return T;
+	Seg c = locate(prefix, S, H, y);
+	return c.j == 0 ? y : y - c.j + c.ts;
+}
+
+// Owner warp of flattened tile x in the balanced split: warp w covers
+// [floor(w*T/W), floor((w+1)*T/W)).
+__device__ __forceinline__ long long owner_warp(long long x, long long T,
+						long long W)
+{
+	return ((x + 1) * W - 1) / T;
+}
+
+template <int N>
+__device__ __forceinline__ void lds_words(uint32_t (&w)[N], const uint8_t *p)
+{
+	if constexpr (N % 4 == 0) {
+#pragma unroll
+		for (int i = 0; i < N / 4; ++i) {
+			uint4 v = reinterpret_cast<const uint4 *>(p)[i];
+			w[4 * i] = v.x;
+			w[4 * i + 1] = v.y;
+			w[4 * i + 2] = v.z;
+			w[4 * i + 3] = v.w;
+		}
+	} else if constexpr (N == 2) {
+		uint2 v = *reinterpret_cast<const uint2 *>(p);
+		w[0] = v.x;
+		w[1] = v.y;
+	} else {
+		w[0] = *reinterpret_cast<const uint32_t *>(p);
+	}
+}
+
+// Block-table entries for 32 consecutive tiles of the warp's stream, one per
+// lane, plus the tile's kv head / sub-tile / valid-token count.
+struct Batch {
+	unsigned long long k, v;
+	int valid;
+	int pack;  // ntok | sub << 8 | h << 16
+};
+
+__device__ __forceinline__ void load_batch(Batch &b, const kllm_decode_args &a,
+					   const int *prefix, const int *slen,
+					   long long xa, int n, int base,
+					   int lane, int tpp)
+{
+	int pos = base + lane;
+	b.k = 0;
+	b.v = 0;
+	b.valid = 0;
+	b.pack = 0;
+	if (pos < n) {
+		Seg c = locate(prefix, a.num_seqs, a.num_kv_heads, xa + pos);
+		int ntok = slen[c.s] - c.j * kTile;
+		ntok = ntok < kTile ? ntok : kTile;
+		int page = c.j / tpp, sub = c.j - page * tpp;
+		const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+				    (size_t)c.s * a.max_blocks + page;
+		b.k = __ldg(&e->k);
+		b.v = __ldg(&e->v);
+		b.valid = __ldg(&e->valid);
+		b.pack = ntok | (sub << 8) | (c.h << 16);
+	}
+}
+
+template <int D>
+__device__ __forceinline__ void load_q(uint32_t (&q)[D / 8],
+				       const kllm_decode_args &a, int s, int h,
+				       int lane)
+{
+	const int g = lane >> 2, c = lane & 3;
+	if (g < a.group) {
+		const uint8_t *p = reinterpret_cast<const uint8_t *>(a.q) +
+			(((size_t)s * a.num_heads + (size_t)h * a.group + g) * D +
+			 (size_t)c * (D / 4)) * 2;
+#pragma unroll
+		for (int i = 0; i < D / 32; ++i) {
+			uint4 v = __ldg(reinterpret_cast<const uint4 *>(p) + i);
+			q[4 * i] = v.x;
+			q[4 * i + 1] = v.y;
+			q[4 * i + 2] = v.z;
+			q[4 * i + 3] = v.w;
+		}
+	} else {
+#pragma unroll
+		for (int i = 0; i < D / 8; ++i)
+			q[i] = 0u;
+	}
+}
+
+// One 16-token tile: scores, online-softmax update and PV accumulation.
+template <int D, int KVT>
+__device__ __forceinline__ void tile_compute(
+    const uint8_t *sK, const uint8_t *sV, const uint32_t *lut, int ntok,
+    const uint32_t (&q)[D / 8], float (&o)[D / 16][4], float &m0, float &m1,
+    float &l0, float &l1, float scale_log2, int lane)
+{
+	using Gm = Geom<D, KVT>;
+	const int g = lane >> 2, c = lane & 3;
+
+	// ---- S^T[tok][head] = K . Q^T ------------------------------------------
+	float s[4] = {0.f, 0.f, 0.f, 0.f};
+	if constexpr (Gm::MX) {
+		constexpr int KW = D / 16;
+		uint32_t k0[KW], k1[KW];
+		lds_words<KW>(k0, sK + g * D + c * (D / 4));
+		lds_words<KW>(k1, sK + (g + 8) * D + c * (D / 4));
+		uint32_t sw0, sw1;
+		if constexpr (D == 128) {
+			sw0 = *reinterpret_cast<const uint32_t *>(sK + kTile * D + g * 16 + c * 4);
+			sw1 = *reinterpret_cast<const uint32_t *>(sK + kTile * D + (g + 8) * 16 + c * 4);
+		} else {
+			sw0 = *reinterpret_cast<const uint16_t *>(sK + kTile * D + g * 8 + c * 2);
+			sw1 = *reinterpret_cast<const uint16_t *>(sK + kTile * D + (g + 8) * 8 + c * 2);
+		}
+#pragma unroll
+		for (int j = 0; j < D / 16; ++j) {
+			const uint32_t sc0 = lut[(sw0 >> (8 * (j >> 1))) & 0xFFu];
+			const uint32_t sc1 = lut[(sw1 >> (8 * (j >> 1))) & 0xFFu];
+			const uint32_t a0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k0[j], false), sc0);
+			const uint32_t a2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k0[j], true), sc0);
+			const uint32_t a1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], false), sc1);
+			const uint32_t a3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], true), sc1);
+			mma_bf16(s, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
+		}
+	} else {
+		constexpr int KW = D / 8;
+		uint32_t k0[KW], k1[KW];
+		lds_words<KW>(k0, sK + (g * D + c * (D / 4)) * 2);
+		lds_words<KW>(k1, sK + ((g + 8) * D + c * (D / 4)) * 2);
+#pragma unroll
+		for (int j = 0; j < D / 16; ++j)
+			mma_bf16(s, k0[2 * j], k1[2 * j], k0[2 * j + 1],
+				 k1[2 * j + 1], q[2 * j], q[2 * j + 1]);
+	}
+
+	// ---- online softmax (log2 domain) ----------------------------------------
+	const bool v0 = g < ntok, v1 = g + 8 < ntok;
+	const float x0 = v0 ? s[0] * scale_log2 : -CUDART_INF_F;  // tok g,   head 2c
+	const float x1 = v0 ? s[1] * scale_log2 : -CUDART_INF_F;  // tok g,   head 2c+1
+	const float x2 = v1 ? s[2] * scale_log2 : -CUDART_INF_F;  // tok g+8, head 2c
+	const float x3 = v1 ? s[3] * scale_log2 : -CUDART_INF_F;  // tok g+8, head 2c+1
+	float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+	for (int off = 4; off < 32; off <<= 1) {
+		t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+		t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+	}
+	const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);  // finite: ntok >= 1
+	const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+	const float p0 = exp2f(x0 - mn0), p2 = exp2f(x2 - mn0);
+	const float p1 = exp2f(x1 - mn1), p3 = exp2f(x3 - mn1);
+	l0 = l0 * al0 + (p0 + p2);
+	l1 = l1 * al1 + (p1 + p3);
+	m0 = mn0;
+	m1 = mn1;
+#pragma unroll
+	for (int mt = 0; mt < D / 16; ++mt) {
+		o[mt][0] *= al0;
+		o[mt][1] *= al1;
+		o[mt][2] *= al0;
+		o[mt][3] *= al1;
+	}
+	const uint32_t b0 = movmatrix_trans(pack_bf16x2(p0, p1));  // tok 2c,2c+1;   head g
+	const uint32_t b1 = movmatrix_trans(pack_bf16x2(p2, p3));  // tok 2c+8,2c+9; head g
+
+	// ---- O^T[dim][head] += V^T . P^T -----------------------------------------
+	const int r0 = 2 * c, r1 = 2 * c + 1, r2 = 2 * c + 8, r3 = 2 * c + 9;
+	if constexpr (Gm::MX) {
+		constexpr int VW = D / 32;
+		uint32_t w0[VW], w1[VW], w2[VW], w3[VW];
+		lds_words<VW>(w0, sV + r0 * D + g * (D / 8));
+		lds_words<VW>(w1, sV + r1 * D + g * (D / 8));
+		lds_words<VW>(w2, sV + r2 * D + g * (D / 8));
+		lds_words<VW>(w3, sV + r3 * D + g * (D / 8));
+		if (ntok < kTile) {  // zero rows past the context (payload 0 == 0.0)
+#pragma unroll
+			for (int i = 0; i < VW; ++i) {
+				if (r0 >= ntok) w0[i] = 0u;
+				if (r1 >= ntok) w1[i] = 0u;
+				if (r2 >= ntok) w2[i] = 0u;
+				if (r3 >= ntok) w3[i] = 0u;
+			}
+		}
+		constexpr int NB = D / 64;  // scale blocks per lane chunk
+		uint32_t s01[NB], s23[NB];
+		const uint8_t *sS = sV + kTile * D;
+#pragma unroll
+		for (int bb = 0; bb < NB; ++bb) {
+			const int col = g * NB + bb;
+			s01[bb] = __byte_perm(lut[sS[r0 * (D / 8) + col]],
+					      lut[sS[r1 * (D / 8) + col]], 0x5410u);
+			s23[bb] = __byte_perm(lut[sS[r2 * (D / 8) + col]],
+					      lut[sS[r3 * (D / 8) + col]], 0x5410u);
+		}
+#pragma unroll
+		for (int i = 0; i < VW; ++i) {
+			const int bb = i >> 1;  // m-tiles 2i, 2i+1 -> dims 4i..4i+3 -> block (4i)/8
+			const uint32_t c01a = __byte_perm(w0[i], w1[i], 0x5140u);
+			const uint32_t c01b = __byte_perm(w0[i], w1[i], 0x7362u);
+			const uint32_t c23a = __byte_perm(w2[i], w3[i], 0x5140u);
+			const uint32_t c23b = __byte_perm(w2[i], w3[i], 0x7362u);
+			mma_bf16(o[2 * i],
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, false), s01[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, true), s01[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, false), s23[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, true), s23[bb]),
+				 b0, b1);
+			mma_bf16(o[2 * i + 1],
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, false), s01[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, true), s01[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, false), s23[bb]),
+				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, true), s23[bb]),
+				 b0, b1);
+		}
+	} else {
+		constexpr int VW = D / 16;
+		uint32_t w0[VW], w1[VW], w2[VW], w3[VW];
+		lds_words<VW>(w0, sV + (r0 * D + g * (D / 8)) * 2);
+		lds_words<VW>(w1, sV + (r1 * D + g * (D / 8)) * 2);
+		lds_words<VW>(w2, sV + (r2 * D + g * (D / 8)) * 2);
+		lds_words<VW>(w3, sV + (r3 * D + g * (D / 8)) * 2);
+		if (ntok < kTile) {  // rows past the context may hold any bits
+#pragma unroll
+			for (int i = 0; i < VW; ++i) {
+				if (r0 >= ntok) w0[i] = 0u;
+				if (r1 >= ntok) w1[i] = 0u;
+				if (r2 >= ntok) w2[i] = 0u;
+				if (r3 >= ntok) w3[i] = 0u;
+			}
+		}
+#pragma unroll
+		for (int mt = 0; mt < D / 16; ++mt)
+			mma_bf16(o[mt], __byte_perm(w0[mt], w1[mt], 0x5410u),
+				 __byte_perm(w0[mt], w1[mt], 0x7632u),
+				 __byte_perm(w2[mt], w3[mt], 0x5410u),
+				 __byte_perm(w2[mt], w3[mt], 0x7632u), b0, b1);
+	}
+}
+
+// Writes one query head's normalised row: bf16 output or fp32 triple.
+// vals[k] = dim (D/8)*g + k.
+template <int D>
+__device__ __forceinline__ void store_head_row(const kllm_decode_args &a,
+					       size_t row, int g,
+					       const float (&vals)[D / 8],
+					       float m_log2, float lsum,
+					       float unbias)
+{
+	const float inv = lsum > 0.f ? unbias / lsum : 0.f;
+	if (a.pm) {
+		float *po = a.po + row * D + (size_t)g * (D / 8);
+#pragma unroll
+		for (int k = 0; k < D / 8; k += 4)
+			*reinterpret_cast<float4 *>(po + k) = make_float4(
+			    vals[k] * inv, vals[k + 1] * inv, vals[k + 2] * inv,
+			    vals[k + 3] * inv);
+		if (g == 0) {
+			a.pm[row] = lsum > 0.f ? m_log2 * 0.69314718055994531f
+					       : -CUDART_INF_F;
+			a.pl[row] = lsum;
+		}
+	} else {
+		uint32_t packed[D / 16];
+#pragma unroll
+		for (int k = 0; k < D / 16; ++k)
+			packed[k] = pack_bf16x2(vals[2 * k] * inv, vals[2 * k + 1] * inv);
+		uint8_t *po = reinterpret_cast<uint8_t *>(a.out) +
+			      (row * D + (size_t)g * (D / 8)) * 2;
+#pragma unroll
+		for (int k = 0; k < D / 16; k += 4)
+			*reinterpret_cast<uint4 *>(po + k * 4) =
+			    make_uint4(packed[k], packed[k + 1], packed[k + 2], packed[k + 3]);
+	}
+}
+
+template <int D>
+__device__ void write_empty_seq(const kllm_decode_args &a, int s, int lane)
+{
+	const size_t rows = (size_t)a.num_heads;
+	const size_t row0 = (size_t)s * a.num_heads;
+	if (a.pm) {
+		for (size_t r = lane; r < rows; r += 32) {
+			a.pm[row0 + r] = -CUDART_INF_F;
+			a.pl[row0 + r] = 0.f;
+		}
+		float4 *po = reinterpret_cast<float4 *>(a.po + row0 * D);
+		for (size_t i = lane; i < rows * D / 4; i += 32)
+			po[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+	} else if (a.out) {
+		uint4 *po = reinterpret_cast<uint4 *>(
+		    reinterpret_cast<uint8_t *>(a.out) + row0 * D * 2);
+		for (size_t i = lane; i < rows * D / 8; i += 32)
+			po[i] = make_uint4(0u, 0u, 0u, 0u);
+	}
+}
+
+// Log-sum-exp merge of the pieces of one segment, run by the warp that
+// finished last. Lane -> (head lane/4, dims (lane%4)*D/4 ..).
+template <int D>
+__device__ void merge_segment(const kllm_decode_args &a, const Seg &sg,
+			      long long seg_x0, long long T, long long W,
+			      float unbias, int lane)
+{
+	const long long w0 = owner_warp(seg_x0, T, W);
+	const long long w1 = owner_warp(seg_x0 + sg.ts - 1, T, W);
+	const int hh = lane >> 2, part = lane & 3;
+	constexpr int NV = D / 4;  // values per lane
+	float acc[NV];
+#pragma unroll
+	for (int i = 0; i < NV; ++i)
+		acc[i] = 0.f;
+	float M = -CUDART_INF_F, L = 0.f;
+	const bool active = hh < a.group;
+
+	for (long long wr = w0; wr <= w1; ++wr) {
+		const long long b = wr * T / W;
+		const int which = (wr == w0 && b != seg_x0) ? 1 : 0;
+		const float *slot = a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
+		if (!active)
+			continue;
+		const float mr = __ldcg(slot + kSlotM + hh);
+		const float lr = __ldcg(slot + kSlotL + hh);
+		if (!(lr > 0.f))
+			continue;
+		const float mn = fmaxf(M, mr);
+		const float fo = exp2f(M - mn), fr = exp2f(mr - mn);
+		L = L * fo + lr * fr;
+		M = mn;
+		const float4 *src = reinterpret_cast<const float4 *>(
+		    slot + kSlotO + hh * D + part * NV);
+#pragma unroll
+		for (int i = 0; i < NV / 4; ++i) {
+			const float4 v = __ldcg(src + i);
+			acc[4 * i] = acc[4 * i] * fo + v.x * fr;
+			acc[4 * i + 1] = acc[4 * i + 1] * fo + v.y * fr;
+			acc[4 * i + 2] = acc[4 * i + 2] * fo + v.z * fr;
+			acc[4 * i + 3] = acc[4 * i + 3] * fo + v.w * fr;
+		}
+	}
+	if (!active)
+		return;
+	const size_t row = (size_t)sg.s * a.num_heads + (size_t)sg.h * a.group + hh;
+	const float inv = L > 0.f ? unbias / L : 0.f;
+	if (a.pm) {
+		float *po = a.po + row * D + part * NV;
+#pragma unroll
+		for (int i = 0; i < NV; i += 4)
+			*reinterpret_cast<float4 *>(po + i) = make_float4(
+			    acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv,
+			    acc[i + 3] * inv);
+		if (part == 0) {
+			a.pm[row] = L > 0.f ? M * 0.69314718055994531f : -CUDART_INF_F;
+			a.pl[row] = L;
+		}
+	} else {
+		uint8_t *po = reinterpret_cast<uint8_t *>(a.out) + (row * D + part * NV) * 2;
+#pragma unroll
+		for (int i = 0; i < NV; i += 8)
+			*reinterpret_cast<uint4 *>(po + i * 2) = make_uint4(
+			    pack_bf16x2(acc[i] * inv, acc[i + 1] * inv),
+			    pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
+			    pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv),
+			    pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
+	}
+}
+
+template <int D, int KVT>
+__global__ void __launch_bounds__(kWarps * 32)
+decode_kernel(const kllm_decode_args a)
+{
+	using Gm = Geom<D, KVT>;
+	extern __shared__ __align__(128) uint8_t smem[];
+	const int S = a.num_seqs, H = a.num_kv_heads;
+	const SmemLayout lay(Gm::STAGE, Gm::NST, S);
+	uint64_t *bars = reinterpret_cast<uint64_t *>(smem + lay.bar);
+	int *meta = reinterpret_cast<int *>(smem + lay.meta);
+	uint32_t *lut = reinterpret_cast<uint32_t *>(smem + lay.lut);
+	int *prefix = reinterpret_cast<int *>(smem + lay.prefix);
+	int *slen = reinterpret_cast<int *>(smem + lay.slen);
+
+	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+	const int tpp = a.block_size / kTile;
+
+	// ---- per-CTA setup: scale LUT, clamped lengths, tile prefix sums -------
+	if constexpr (Gm::MX)
+		for (int i = tid; i < 256; i += blockDim.x)
+			lut[i] = mx_scale_lut_entry((uint32_t)i);
+	{
+		bool too_long = false;
+		const int cap = a.max_blocks * a.block_size;
+		for (int s = tid; s < S; s += blockDim.x) {
+			int L = a.seq_lens[s];
+			L = L < 0 ? 0 : L;
+			if (L > cap) {
+				L = cap;
+				too_long = true;
+			}
+			slen[s] = L;
+		}
+		if (too_long && a.err && blockIdx.x == 0)
+			atomicOr(a.err, 0x1u);
+	}
+	if (lane == 0)
+		for (int i = 0; i < Gm::NST; ++i)
+			mbar_init(&bars[warp * Gm::NST + i], 1);
+	__syncthreads();
+	if (warp == 0) {
+		int run = 0;
+		for (int base = 0; base < S; base += 32) {
+			const int s = base + lane;
+			const int t = s < S ? (slen[s] + kTile - 1) / kTile : 0;
+			int v = t;
+#pragma unroll
+			for (int off = 1; off < 32; off <<= 1) {
+				const int n = __shfl_up_sync(0xffffffffu, v, off);
+				if (lane >= off)
+					v += n;
+			}
+			if (s < S)
+				prefix[s] = run + v - t;
+			run += __shfl_sync(0xffffffffu, v, 31);
+		}
+		if (lane == 0)
+			prefix[S] = run;
+	}
+	if (lane == 0)
+		fence_mbar_init();
+	__syncthreads();
+
+	const long long T = (long long)prefix[S] * H;
+	const int w = blockIdx.x * kWarps + warp;
+
+	for (int s = w; s < S; s += a.total_warps)
+		if (prefix[s + 1] == prefix[s])
+			write_empty_seq<D>(a, s, lane);
+	if (T == 0)
+		return;
+
+	const long long W = a.split ? (T < a.total_warps ? T : a.total_warps)
+				    : a.total_warps;
+	if (w >= W)
+		return;
+	long long xa, xb;
+	if (a.split) {
+		xa = (long long)w * T / W;
+		xb = (long long)(w + 1) * T / W;
+	} else {
+		xa = seg_start_at_or_after(prefix, S, H, T, (long long)w * T / W);
+		xb = seg_start_at_or_after(prefix, S, H, T, (long long)(w + 1) * T / W);
+	}
+	if (xa >= xb)
+		return;
+	const int n = (int)(xb - xa);
+
+	uint8_t *wst = smem + lay.stage + (size_t)warp * Gm::NST * Gm::STAGE;
+	uint64_t *wbar = bars + warp * Gm::NST;
+	int *wmeta = meta + warp * Gm::NST;
+	const uint64_t policy = l2_evict_first_policy();
+	const size_t sec = Gm::MX ? (size_t)a.block_size * D * 9 / 8
+				  : (size_t)a.block_size * D * 2;
+	const float unbias = Gm::MX ? kMxUnbias : 1.f;
+
+	// ---- producer: block-table batches and the bulk-copy ring --------------
+	Batch cur, nxt;
+	load_batch(cur, a, prefix, slen, xa, n, 0, lane, tpp);
+	load_batch(nxt, a, prefix, slen, xa, n, 32, lane, tpp);
+	int pb = 0;
+
+	auto issue = [&](int pos) {
+		int bi = pos - pb;
+		if (bi >= 32) {
+			cur = nxt;
+			pb += 32;
+			bi -= 32;
+			load_batch(nxt, a, prefix, slen, xa, n, pb + 32, lane, tpp);
+		}
+		const unsigned long long ek = __shfl_sync(0xffffffffu, cur.k, bi);
+		const unsigned long long ev = __shfl_sync(0xffffffffu, cur.v, bi);
+		const int valid = __shfl_sync(0xffffffffu, cur.valid, bi);
+		const int pack = __shfl_sync(0xffffffffu, cur.pack, bi);
+		if (lane == 0) {
+			const int st = pos % Gm::NST;
+			const int ntok = pack & 0xFF, sub = (pack >> 8) & 0xFF, h = pack >> 16;
+			const bool present = valid && ek != 0ull;
+			const bool aligned = ((ek | ev) & 15ull) == 0ull;
+			if (present && !aligned && a.err)
+				atomicOr(a.err, 0x2u);
+			const bool ok = present && aligned && ntok > 0;
+			wmeta[st] = ok ? ntok : 0;
+			uint64_t *bar = &wbar[st];
+			if (ok) {
+				mbar_arrive_expect_tx(bar, Gm::STAGE);
+				uint8_t *dK = wst + (size_t)st * Gm::STAGE;
+				uint8_t *dV = dK + Gm::KV;
+				const uint8_t *sK = reinterpret_cast<const uint8_t *>(ek) +
+						    a.layer_off + (size_t)h * sec;
+				const uint8_t *sV = reinterpret_cast<const uint8_t *>(ev) +
+						    a.layer_off + (size_t)h * sec;
+				if (Gm::MX && tpp == 1) {  // payload + scales contiguous
+					bulk_g2s_stream(dK, sK, Gm::KV, bar, policy);
+					bulk_g2s_stream(dV, sV, Gm::KV, bar, policy);
+				} else {
+					bulk_g2s_stream(dK, sK + (size_t)sub * Gm::PAY, Gm::PAY, bar, policy);
+					bulk_g2s_stream(dV, sV + (size_t)sub * Gm::PAY, Gm::PAY, bar, policy);
+					if (Gm::MX) {
+						const size_t so = (size_t)a.block_size * D + (size_t)sub * Gm::SCL;
+						bulk_g2s_stream(dK + Gm::PAY, sK + so, Gm::SCL, bar, policy);
+						bulk_g2s_stream(dV + Gm::PAY, sV + so, Gm::SCL, bar, policy);
+					}
+				}
+			} else {
+				mbar_arrive(bar);
+			}
+		}
+	};
+
+	int p = 0;
+	for (; p < n && p < Gm::NST - 1; ++p)
+		issue(p);
+
+	// ---- consumer ------------------------------------------------------------
+	Seg cc = locate(prefix, S, H, xa);
+	long long piece_x0 = xa;
+	int piece_j0 = cc.j;
+	uint32_t q[D / 8];
+	load_q<D>(q, a, cc.s, cc.h, lane);
+	float o[D / 16][4];
+#pragma unroll
+	for (int mt = 0; mt < D / 16; ++mt)
+		o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+	float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+	const int g = lane >> 2, c = lane & 3;
+
+	for (int i = 0; i < n; ++i) {
+		if (p < n) {
+			issue(p);
+			++p;
+		}
+		const int st = i % Gm::NST;
+		if (!mbar_wait(&wbar[st], (uint32_t)((i / Gm::NST) & 1))) {
+			if (lane == 0 && a.err)
+				atomicOr(a.err, KLLM_ERR_TIMEOUT_BIT);
+			return;
+		}
+		const int ntok = *reinterpret_cast<volatile int *>(&wmeta[st]);
+		if (ntok > 0) {
+			const uint8_t *sK = wst + (size_t)st * Gm::STAGE;
+			tile_compute<D, KVT>(sK, sK + Gm::KV, lut, ntok, q, o, m0,
+					     m1, l0, l1, a.scale_log2, lane);
+		}
+		__syncwarp();
+
+		const bool seg_end = cc.j + 1 == cc.ts;
+		const bool last = i + 1 == n;
+		if (!(seg_end || last)) {
+			++cc.j;
+			continue;
+		}
+
+		// ---- piece finished: normalise, or publish a partial -------------
+		float L0 = l0, L1 = l1;
+#pragma unroll
+		for (int off = 4; off < 32; off <<= 1) {
+			L0 += __shfl_xor_sync(0xffffffffu, L0, off);
+			L1 += __shfl_xor_sync(0xffffffffu, L1, off);
+		}
+		const bool full = piece_j0 == 0 && seg_end;
+		const size_t row0 = (size_t)cc.s * a.num_heads + (size_t)cc.h * a.group;
+		if (full) {
+#pragma unroll
+			for (int hp = 0; hp < 2; ++hp) {
+				const int hh = 2 * c + hp;
+				if (hh < a.group) {
+					float vals[D / 8];
+#pragma unroll
+					for (int mt = 0; mt < D / 16; ++mt) {
+						vals[2 * mt] = o[mt][hp];
+						vals[2 * mt + 1] = o[mt][2 + hp];
+					}
+					store_head_row<D>(a, row0 + hh, g, vals,
+							  hp ? m1 : m0, hp ? L1 : L0, unbias);
+				}
+			}
+		} else {
+			const int which = piece_x0 == xa ? 0 : 1;
+			float *slot = a.ws_part + ((size_t)w * 2 + which) * KLLM_SLOT_FLOATS;
+#pragma unroll
+			for (int hp = 0; hp < 2; ++hp) {
+				const int hh = 2 * c + hp;
+				if (hh < a.group) {
+					float *dst = slot + kSlotO + hh * D + g * (D / 8);
+#pragma unroll
+					for (int mt = 0; mt < D / 16; mt += 2)
+						*reinterpret_cast<float4 *>(dst + 2 * mt) =
+						    make_float4(o[mt][hp], o[mt][2 + hp],
+								o[mt + 1][hp], o[mt + 1][2 + hp]);
+					if (g == 0) {
+						slot[kSlotM + hh] = hp ? m1 : m0;
+						slot[kSlotL + hh] = hp ? L1 : L0;
+					}
+				}
+			}
+			__threadfence();
+			__syncwarp();
+			const long long seg_x0 = piece_x0 - piece_j0;
+			const long long npieces = owner_warp(seg_x0 + cc.ts - 1, T, W) -
+						  owner_warp(seg_x0, T, W) + 1;
+			unsigned old = 0;
+			unsigned *cnt = a.ws_cnt + (size_t)cc.s * H + cc.h;
+			if (lane == 0)
+				old = atomicAdd(cnt, 1u);
+			old = __shfl_sync(0xffffffffu, old, 0);
+			if ((long long)old == npieces - 1) {
+				__threadfence();
+				merge_segment<D>(a, cc, seg_x0, T, W, unbias, lane);
+				if (lane == 0)
+					*cnt = 0u;  // ready for the next launch
+			}
+		}
+
+		if (last)
+			break;
+		// next segment
+		cc.j = 0;
+		if (++cc.h == H) {
+			cc.h = 0;
+			do {
+				++cc.s;
+			} while (prefix[cc.s + 1] == prefix[cc.s]);
+			cc.ts = prefix[cc.s + 1] - prefix[cc.s];
+		}
+		piece_j0 = 0;
+		piece_x0 = xa + i + 1;
+		load_q<D>(q, a, cc.s, cc.h, lane);
+#pragma unroll
+		for (int mt = 0; mt < D / 16; ++mt)
+			o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+		m0 = m1 = -CUDART_INF_F;
+		l0 = l1 = 0.f;
+	}
+}
+
+template <int D, int KVT>
+struct Launcher {
+	static size_t smem(int S)
+	{
+		using Gm = Geom<D, KVT>;
+		return SmemLayout(Gm::STAGE, Gm::NST, S).total;
+	}
+	static cudaError_t prepare(int S)
+	{
+		return cudaFuncSetAttribute(decode_kernel<D, KVT>,
+					    cudaFuncAttributeMaxDynamicSharedMemorySize,
+					    (int)smem(S));
+	}
+	static int occupancy(int S)
+	{
+		if (prepare(S) != cudaSuccess)
+			return 0;
+		int n = 0;
+		if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+			&n, decode_kernel<D, KVT>, kWarps * 32, smem(S)) != cudaSuccess)
+			return 0;
+		return n;
+	}
+	static cudaError_t launch(const kllm_decode_args &a, int grid,
+				  cudaStream_t st)
+	{
+		cudaError_t e = prepare(a.num_seqs);
+		if (e != cudaSuccess)
+			return e;
+		decode_kernel<D, KVT><<<grid, kWarps * 32, smem(a.num_seqs), st>>>(a);
+		return cudaGetLastError();
+	}
+};
+
+}  // namespace
+}  // namespace kllm
+
+using namespace kllm;
+
+extern "C" size_t kllm_decode_smem_bytes(int head_dim, int kv_dtype, int num_seqs)
+{
+	if (head_dim == 128)
+		return kv_dtype ? Launcher<128, 1>::smem(num_seqs) : Launcher<128, 0>::smem(num_seqs);
+	if (head_dim == 64)
+		return kv_dtype ? Launcher<64, 1>::smem(num_seqs) : Launcher<64, 0>::smem(num_seqs);
+	return 0;
+}
+
+extern "C" int kllm_decode_ctas_per_sm(int head_dim, int kv_dtype, int num_seqs)
+{
+	if (head_dim == 128)
+		return kv_dtype ? Launcher<128, 1>::occupancy(num_seqs)
+				: Launcher<128, 0>::occupancy(num_seqs);
+	if (head_dim == 64)
+		return kv_dtype ? Launcher<64, 1>::occupancy(num_seqs)
+				: Launcher<64, 0>::occupancy(num_seqs);
+	return 0;
+}
+
+extern "C" int kllm_decode_launch(const struct kllm_decode_args *a, int grid,
+				  void *stream)
+{
+	cudaStream_t st = static_cast<cudaStream_t>(stream);
+	cudaError_t e;
+	if (a->head_dim == 128)
+		e = a->kv_dtype ? Launcher<128, 1>::launch(*a, grid, st)
+				: Launcher<128, 0>::launch(*a, grid, st);
+	else if (a->head_dim == 64)
+		e = a->kv_dtype ? Launcher<64, 1>::launch(*a, grid, st)
+				: Launcher<64, 0>::launch(*a, grid, st);
+	else
+		e = cudaErrorInvalidValue;
+	return (int)e;
+}
