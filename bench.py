@@ -73,7 +73,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -160,6 +160,7 @@ class DecodeRig:
                     torch.bfloat16)
                 rc = self.be.append(k=k.data_ptr(), v=v.data_ptr(), token_seq=ts.data_ptr(),
                                     token_pos=tp.data_ptr(), num_tokens=b - a,
+                                    num_seqs=self.B,
                                     block_tables=self.table.data_ptr(),
                                     max_blocks_per_seq=self.plan.max_blocks,
                                     num_kv_heads=c.hkv, head_dim=c.d, block_size=c.block,
@@ -231,6 +232,9 @@ def run_kllm(args) -> None:
     be = kb.Backend()
     if be.backend != kb.KLLM_GPU_CUDA:
         raise RuntimeError("libkllm_gpu: no sm_100 device")
+    # torch work (data generation, events) and the library's launches share
+    # the context stream, so every CUDA event brackets the library's kernels
+    torch.cuda.set_stream(be.torch_stream())
 
     cfg = wl.CONFIGS[args.config]
     if args.layers:
@@ -364,6 +368,8 @@ def run_kllm(args) -> None:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
     be.close()
     if world > 1:
         dist.destroy_process_group()
@@ -466,8 +472,8 @@ def run_reference(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
     ap.add_argument("--config", default=wl.C3.name, choices=list(wl.CONFIGS))
     ap.add_argument("--seed", type=int, default=0)

@@ -132,6 +132,7 @@ int kllm_gpu_paged_attention_cuda(
 #define KLLM_ERR_SEQ_TOO_LONG   0x1u  /* seq_len > max_blocks_per_seq * block_size: clamped */
 #define KLLM_ERR_MISALIGNED     0x2u  /* page pointer not 16-byte aligned: page skipped */
 #define KLLM_ERR_APPEND_NOPAGE  0x4u  /* append target page invalid / position out of table */
+#define KLLM_ERR_TIMEOUT        0x8u  /* a bounded device-side wait expired; the warp stopped */
 
 /* KV page formats. One page holds `block_size` tokens of one layer.
  *
@@ -199,8 +200,9 @@ uint64_t kllm_gpu_decode_workspace_size(struct kllm_gpu_ctx *ctx, int num_seqs,
 
 /* KV append with quantize-on-write. Token i (row i of k/v) goes to position
  * token_pos[i] of sequence token_seq[i]: page = block_tables[seq][pos /
- * block_size], slot = pos % block_size. Rows whose page entry is invalid are
- * skipped and flagged with KLLM_ERR_APPEND_NOPAGE.
+ * block_size], slot = pos % block_size. Rows whose sequence or position is out
+ * of the table, or whose page entry is invalid, are skipped and flagged with
+ * KLLM_ERR_APPEND_NOPAGE.
  *   BF16:            bytes copied.
  *   MX_FP8_E4M3:     per 8 elements: amax; scale = smallest E4M3 >= amax/448
  *                    (0 when amax == 0); payload = RNE-satfinite E4M3 of
@@ -215,7 +217,9 @@ struct kllm_gpu_kv_append_params {
 	const int *token_seq;        /* int32 [num_tokens] */
 	const int *token_pos;        /* int32 [num_tokens] */
 	int num_tokens;
-	const void *block_tables;    /* kllm_block_table_entry [.][max_blocks_per_seq] */
+	int num_seqs;                /* rows of block_tables; token_seq outside
+	                                [0, num_seqs) is skipped and flagged */
+	const void *block_tables;    /* kllm_block_table_entry [num_seqs][max_blocks_per_seq] */
 	int max_blocks_per_seq;
 	int num_kv_heads;
 	int head_dim;

@@ -25,7 +25,10 @@ def be():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     b = Backend()
     assert b.backend == kb.KLLM_GPU_CUDA, "libkllm_gpu found no sm_100 device"
+    torch.cuda.set_stream(b.torch_stream())
     yield b
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
     b.close()
 
 
@@ -232,4 +235,5 @@ def test_rejects_bad_shapes(be):
     assert be.decode_v2(**dc.decode_kwargs(num_heads=30)) == kb.EINVAL
     assert be.decode_v2(**dc.decode_kwargs(block_size=24)) == kb.ENOSYS
     assert be.decode_v2(**dc.decode_kwargs(kv_dtype=7)) == kb.ENOSYS
-    assert be.decode_v2(**dc.decode_kwargs(layer_stride=8, layer=1)) == kb.EINVAL
+    assert be.decode_v2(**dc.decode_kwargs(layer_stride=8)) == kb.EINVAL
+    assert be.decode_v2(**dc.decode_kwargs(layer=-1)) == kb.EINVAL

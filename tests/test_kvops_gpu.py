@@ -22,7 +22,10 @@ def be():
     assert torch.cuda.is_available()
     b = Backend()
     assert b.backend == kb.KLLM_GPU_CUDA
+    torch.cuda.set_stream(b.torch_stream())
     yield b
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
     b.close()
 
 
@@ -94,7 +97,8 @@ def test_append_bit_exact(be, kv, extreme):
     pd = torch.from_numpy(pos).cuda()
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = be.append(k=kd.data_ptr(), v=vd.data_ptr(), token_seq=sd.data_ptr(),
-                   token_pos=pd.data_ptr(), num_tokens=len(seq), block_tables=td.data_ptr(),
+                   token_pos=pd.data_ptr(), num_tokens=len(seq), num_seqs=len(plan.seq_lens),
+                   block_tables=td.data_ptr(),
                    max_blocks_per_seq=plan.max_blocks, num_kv_heads=cfg.hkv, head_dim=cfg.d,
                    block_size=cfg.block, kv_dtype=kv, err_word=err.data_ptr(),
                    stream=_stream())
@@ -124,7 +128,8 @@ def test_append_missing_page_flag(be):
     pd = torch.from_numpy(pos).cuda()
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = be.append(k=kd.data_ptr(), v=kd.data_ptr(), token_seq=sd.data_ptr(),
-                   token_pos=pd.data_ptr(), num_tokens=len(seq), block_tables=td.data_ptr(),
+                   token_pos=pd.data_ptr(), num_tokens=len(seq), num_seqs=len(plan.seq_lens),
+                   block_tables=td.data_ptr(),
                    max_blocks_per_seq=plan.max_blocks, num_kv_heads=cfg.hkv, head_dim=cfg.d,
                    block_size=cfg.block, kv_dtype=1, err_word=err.data_ptr(), stream=_stream())
     assert rc == 0
@@ -226,10 +231,13 @@ def test_append_then_decode(be):
     k = wl.normal_bf16(11, wl.ST_PK, 0, (len(pos), cfg.hkv, cfg.d))
     v = wl.normal_bf16(11, wl.ST_PV, 0, (len(pos), cfg.hkv, cfg.d))
     oracle.kv_append(k, v, seq, pos, hc.host_table(), mb, cfg.hkv, cfg.d, cfg.block, 1)
-    rc = be.append(k=torch.from_numpy(k.view(np.int16).copy()).cuda().data_ptr(),
-                   v=torch.from_numpy(v.view(np.int16).copy()).cuda().data_ptr(),
-                   token_seq=torch.from_numpy(seq).cuda().data_ptr(),
-                   token_pos=torch.from_numpy(pos).cuda().data_ptr(), num_tokens=len(seq),
+    # keep every device buffer referenced until the launch has completed
+    kd = torch.from_numpy(k.view(np.int16).copy()).cuda()
+    vd = torch.from_numpy(v.view(np.int16).copy()).cuda()
+    sd = torch.from_numpy(seq).cuda()
+    pd = torch.from_numpy(pos).cuda()
+    rc = be.append(k=kd.data_ptr(), v=vd.data_ptr(), token_seq=sd.data_ptr(),
+                   token_pos=pd.data_ptr(), num_tokens=len(seq), num_seqs=len(lens),
                    block_tables=dc.table.data_ptr(), max_blocks_per_seq=mb,
                    num_kv_heads=cfg.hkv, head_dim=cfg.d, block_size=16, kv_dtype=1,
                    stream=_stream())

@@ -55,6 +55,7 @@ struct kllm_append_args {
 	const void *k, *v;
 	const int *token_seq, *token_pos;
 	int num_tokens;
+	int num_seqs;
 	const void *table;
 	int max_blocks, num_kv_heads, head_dim, block_size, kv_dtype;
 	uint64_t layer_off;

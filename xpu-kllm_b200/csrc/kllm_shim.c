@@ -378,13 +378,6 @@ static int check_decode_shape(int num_seqs, int num_heads, int num_kv_heads,
 	return KLLM_OK;
 }
 
-static uint64_t page_bytes(int kv_dtype, int bs, int d, int hkv)
-{
-	uint64_t sec = kv_dtype == KLLM_KV_MX_FP8_E4M3 ?
-		(uint64_t)bs * d + (uint64_t)bs * (d / 8) : (uint64_t)bs * d * 2;
-	return sec * hkv;
-}
-
 /* Launches one decode over sequences [s0, s0+ns) of the batch. */
 static int decode_chunk(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *a,
 			int split, float *ws_part, unsigned *ws_cnt,
@@ -613,7 +606,8 @@ int kllm_gpu_kv_append_v2(struct kllm_gpu_ctx *ctx,
 		return fail(ctx, KLLM_EINVAL);
 	if (!ready(ctx))
 		return fail(ctx, KLLM_ENODEV);
-	if (p->num_tokens < 0 || p->num_kv_heads <= 0 || p->max_blocks_per_seq <= 0)
+	if (p->num_tokens < 0 || p->num_seqs <= 0 || p->num_kv_heads <= 0 ||
+	    p->max_blocks_per_seq <= 0)
 		return fail(ctx, KLLM_EINVAL);
 	if (p->head_dim <= 0 || p->head_dim % 8 || p->head_dim > 1024)
 		return fail(ctx, KLLM_ENOSYS);
@@ -634,6 +628,7 @@ int kllm_gpu_kv_append_v2(struct kllm_gpu_ctx *ctx,
 	a.token_seq = p->token_seq;
 	a.token_pos = p->token_pos;
 	a.num_tokens = p->num_tokens;
+	a.num_seqs = p->num_seqs;
 	a.table = p->block_tables;
 	a.max_blocks = p->max_blocks_per_seq;
 	a.num_kv_heads = p->num_kv_heads;

@@ -85,7 +85,7 @@ __global__ void append_kernel(const kllm_append_args a)
 
 	const int seq = a.token_seq[i], pos = a.token_pos[i];
 	const int blk = pos >= 0 ? pos / a.block_size : -1;
-	if (seq < 0 || blk < 0 || blk >= a.max_blocks) {
+	if (seq < 0 || seq >= a.num_seqs || blk < 0 || blk >= a.max_blocks) {
 		if (a.err && b == 0)
 			atomicOr(a.err, 0x4u);
 		return;

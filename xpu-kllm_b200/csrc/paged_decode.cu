@@ -25,8 +25,8 @@
 // tiles ahead; block-table entries are prefetched 32 tiles ahead by the whole
 // warp. The G query heads of the segment share every K/V byte:
 //   S^T[16 tok x 8 heads] = K_tile[16 x D] . Q^T   (mma.m16n8k16, bf16)
-//   P^T -> bf16, transposed in registers (movmatrix)
-//   O^T[D x 8 heads] += V_tile^T[D x 16] . P^T     (mma.m16n8k16, bf16)
+//   P^T -> bf16 hi + bf16 lo, transposed in registers (movmatrix)
+//   O^T[D x 8 heads] += V_tile^T[D x 16] . (P_hi^T + P_lo^T)  (2 x mma.m16n8k16)
 // MX-FP8 tiles are dequantised in registers to bf16 exactly (see
 // kllm_device.cuh). Dimensions are permuted consistently inside each
 // contraction so that every lane reads contiguous 16-byte runs of shared
@@ -53,7 +53,8 @@ struct Geom {
 	static constexpr int SCL = MX ? kTile * D / 8 : 0;          // scales / tile
 	static constexpr int KV = PAY + SCL;                        // one of K, V
 	static constexpr int STAGE = 2 * KV;
-	static constexpr int NST = MX ? 4 : 3;                      // ring depth
+	static constexpr int NST = 3;                               // ring depth
+	static constexpr int MIN_CTAS = MX ? 4 : 2;                 // per SM (16 / 8 warps)
 };
 
 struct DevEntry {  // userspace/gpu/paged_attention.cu:18-22 (24 bytes)
@@ -214,6 +215,7 @@ __device__ __forceinline__ void tile_compute(
 
 	// ---- S^T[tok][head] = K . Q^T ------------------------------------------
 	float s[4] = {0.f, 0.f, 0.f, 0.f};
+	float s2[4] = {0.f, 0.f, 0.f, 0.f};  // odd k-steps: halves the MMA chain
 	if constexpr (Gm::MX) {
 		constexpr int KW = D / 16;
 		uint32_t k0[KW], k1[KW];
@@ -235,7 +237,10 @@ __device__ __forceinline__ void tile_compute(
 			const uint32_t a2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k0[j], true), sc0);
 			const uint32_t a1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], false), sc1);
 			const uint32_t a3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], true), sc1);
-			mma_bf16(s, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
+			if (j & 1)
+				mma_bf16(s2, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
+			else
+				mma_bf16(s, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
 		}
 	} else {
 		constexpr int KW = D / 8;
@@ -243,10 +248,18 @@ __device__ __forceinline__ void tile_compute(
 		lds_words<KW>(k0, sK + (g * D + c * (D / 4)) * 2);
 		lds_words<KW>(k1, sK + ((g + 8) * D + c * (D / 4)) * 2);
 #pragma unroll
-		for (int j = 0; j < D / 16; ++j)
-			mma_bf16(s, k0[2 * j], k1[2 * j], k0[2 * j + 1],
-				 k1[2 * j + 1], q[2 * j], q[2 * j + 1]);
+		for (int j = 0; j < D / 16; ++j) {
+			if (j & 1)
+				mma_bf16(s2, k0[2 * j], k1[2 * j], k0[2 * j + 1],
+					 k1[2 * j + 1], q[2 * j], q[2 * j + 1]);
+			else
+				mma_bf16(s, k0[2 * j], k1[2 * j], k0[2 * j + 1],
+					 k1[2 * j + 1], q[2 * j], q[2 * j + 1]);
+		}
 	}
+#pragma unroll
+	for (int i = 0; i < 4; ++i)
+		s[i] += s2[i];
 
 	// ---- online softmax (log2 domain) ----------------------------------------
 	const bool v0 = g < ntok, v1 = g + 8 < ntok;
@@ -275,8 +288,17 @@ __device__ __forceinline__ void tile_compute(
 		o[mt][2] *= al0;
 		o[mt][3] *= al1;
 	}
-	const uint32_t b0 = movmatrix_trans(pack_bf16x2(p0, p1));  // tok 2c,2c+1;   head g
-	const uint32_t b1 = movmatrix_trans(pack_bf16x2(p2, p3));  // tok 2c+8,2c+9; head g
+	// P as bf16 hi + bf16 lo (16 significant bits): a bf16-only P misses the
+	// 1e-3 absolute bound on outputs built from large, cancelling V values.
+	const uint32_t h01 = pack_bf16x2(p0, p1), h23 = pack_bf16x2(p2, p3);
+	const uint32_t l01 = pack_bf16x2(p0 - __uint_as_float(h01 << 16),
+					 p1 - __uint_as_float(h01 & 0xFFFF0000u));
+	const uint32_t l23 = pack_bf16x2(p2 - __uint_as_float(h23 << 16),
+					 p3 - __uint_as_float(h23 & 0xFFFF0000u));
+	const uint32_t b0 = movmatrix_trans(h01);   // tok 2c,2c+1;   head g
+	const uint32_t b1 = movmatrix_trans(h23);   // tok 2c+8,2c+9; head g
+	const uint32_t c0 = movmatrix_trans(l01);
+	const uint32_t c1 = movmatrix_trans(l23);
 
 	// ---- O^T[dim][head] += V^T . P^T -----------------------------------------
 	const int r0 = 2 * c, r1 = 2 * c + 1, r2 = 2 * c + 8, r3 = 2 * c + 9;
@@ -314,18 +336,18 @@ __device__ __forceinline__ void tile_compute(
 			const uint32_t c01b = __byte_perm(w0[i], w1[i], 0x7362u);
 			const uint32_t c23a = __byte_perm(w2[i], w3[i], 0x5140u);
 			const uint32_t c23b = __byte_perm(w2[i], w3[i], 0x7362u);
-			mma_bf16(o[2 * i],
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, false), s01[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, true), s01[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, false), s23[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, true), s23[bb]),
-				 b0, b1);
-			mma_bf16(o[2 * i + 1],
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, false), s01[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, true), s01[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, false), s23[bb]),
-				 bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, true), s23[bb]),
-				 b0, b1);
+			const uint32_t e0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, false), s01[bb]);
+			const uint32_t e1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, true), s01[bb]);
+			const uint32_t e2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, false), s23[bb]);
+			const uint32_t e3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, true), s23[bb]);
+			mma_bf16(o[2 * i], e0, e1, e2, e3, b0, b1);
+			mma_bf16(o[2 * i], e0, e1, e2, e3, c0, c1);
+			const uint32_t f0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, false), s01[bb]);
+			const uint32_t f1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, true), s01[bb]);
+			const uint32_t f2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, false), s23[bb]);
+			const uint32_t f3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, true), s23[bb]);
+			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, b0, b1);
+			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, c0, c1);
 		}
 	} else {
 		constexpr int VW = D / 16;
@@ -344,11 +366,14 @@ __device__ __forceinline__ void tile_compute(
 			}
 		}
 #pragma unroll
-		for (int mt = 0; mt < D / 16; ++mt)
-			mma_bf16(o[mt], __byte_perm(w0[mt], w1[mt], 0x5410u),
-				 __byte_perm(w0[mt], w1[mt], 0x7632u),
-				 __byte_perm(w2[mt], w3[mt], 0x5410u),
-				 __byte_perm(w2[mt], w3[mt], 0x7632u), b0, b1);
+		for (int mt = 0; mt < D / 16; ++mt) {
+			const uint32_t e0 = __byte_perm(w0[mt], w1[mt], 0x5410u);
+			const uint32_t e1 = __byte_perm(w0[mt], w1[mt], 0x7632u);
+			const uint32_t e2 = __byte_perm(w2[mt], w3[mt], 0x5410u);
+			const uint32_t e3 = __byte_perm(w2[mt], w3[mt], 0x7632u);
+			mma_bf16(o[mt], e0, e1, e2, e3, b0, b1);
+			mma_bf16(o[mt], e0, e1, e2, e3, c0, c1);
+		}
 	}
 }
 
@@ -480,7 +505,7 @@ __device__ void merge_segment(const kllm_decode_args &a, const Seg &sg,
 }
 
 template <int D, int KVT>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, Geom<D, KVT>::MIN_CTAS)
 decode_kernel(const kllm_decode_args a)
 {
 	using Gm = Geom<D, KVT>;

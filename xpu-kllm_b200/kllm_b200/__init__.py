@@ -50,7 +50,7 @@ class AttnParamsV2(Structure):
 class KvAppendParams(Structure):
     _fields_ = [("struct_size", c_uint32), ("flags", c_uint32), ("k", c_void_p),
                 ("v", c_void_p), ("token_seq", c_void_p), ("token_pos", c_void_p),
-                ("num_tokens", c_int), ("block_tables", c_void_p),
+                ("num_tokens", c_int), ("num_seqs", c_int), ("block_tables", c_void_p),
                 ("max_blocks_per_seq", c_int), ("num_kv_heads", c_int), ("head_dim", c_int),
                 ("block_size", c_int), ("kv_dtype", c_int), ("layer", c_int),
                 ("layer_stride", c_uint64), ("err_word", c_void_p), ("stream", c_void_p)]
@@ -152,6 +152,14 @@ class Backend:
     @property
     def stream(self) -> int:
         return self.lib.kllm_gpu_get_stream(self.ctx) or 0
+
+    def torch_stream(self):
+        """The context's stream as a torch stream. Callers that mix torch ops
+        with this library make it torch's current stream, so both are
+        ordered on one stream (a NULL stream argument selects the context
+        stream, userspace/gpu/gpu_attention.c:82, not torch's default)."""
+        import torch
+        return torch.cuda.ExternalStream(self.stream)
 
     def stats(self) -> Stats:
         s = Stats()
