@@ -194,6 +194,23 @@ struct kllm_gpu_attention_params_v2 {
 int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
 				const struct kllm_gpu_attention_params_v2 *p);
 
+/* Allocation-free variant of kllm_gpu_paged_attention_v2 (no counterpart in
+ * the reference). For callers that must not allocate device memory, such as
+ * a polling reactor thread that runs with a zero-allocation rule: cudaMalloc
+ * can stall it and can fail once the KV arena owns the GPU's memory, and a
+ * context cannot be created there because kllm_gpu_create allocates its
+ * workspace. Needs no context; the caller passes inputs and outputs (the
+ * device is the one `stream` belongs to, or the current device when stream
+ * is NULL). Split-KV scratch lives in a fixed 16 MiB device array inside the
+ * library, present on every GPU that loads it until the process exits. The
+ * first call on a device looks up that array's address (a runtime query):
+ * make it before starting any stream capture on that device. Every call
+ * shares the array, so calls that overlap on the GPU race; serialise them.
+ * Limit: num_seqs * num_kv_heads <= 65536, else KLLM_ENOSPC. The workspace
+ * fields of *p are ignored. */
+int kllm_gpu_paged_attention_v2_noalloc(
+    const struct kllm_gpu_attention_params_v2 *p);
+
 /* Bytes of workspace a split-KV decode needs on this context's device. */
 uint64_t kllm_gpu_decode_workspace_size(struct kllm_gpu_ctx *ctx, int num_seqs,
 					int num_kv_heads);

@@ -84,6 +84,7 @@ _SIGNATURES = [
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float,
       c_void_p]),
     ("kllm_gpu_paged_attention_v2", c_int, [c_void_p, POINTER(AttnParamsV2)]),
+    ("kllm_gpu_paged_attention_v2_noalloc", c_int, [POINTER(AttnParamsV2)]),
     ("kllm_gpu_decode_workspace_size", c_uint64, [c_void_p, c_int, c_int]),
     ("kllm_gpu_kv_append_v2", c_int, [c_void_p, POINTER(KvAppendParams)]),
     ("kllm_gpu_gather_debug", c_int, [c_void_p, POINTER(GatherParams)]),
