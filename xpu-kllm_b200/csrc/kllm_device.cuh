@@ -157,6 +157,22 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2_raw(uint32_t w, bool hi)
 	return ((x & 0x7F007F00u) >> 4) | (x & 0x80008000u);
 }
 
+// Four E4M3 bytes of w (b0..b3, low to high) -> two bf16x2 words of
+// e4m3 * 2^-120: lo = (b0, b1), hi = (b2, b3). Per byte the bf16 low byte is
+// (b & 0x0F) << 4 and the high byte is (b & 0x80) | (b >> 4 & 0x07); both are
+// built for all four bytes at once and interleaved with two byte permutes.
+// k16 = 16 and k2p28 = 2^28 are passed as runtime values so the shifts are
+// issued as integer multiplies (FMA pipe), keeping the ALU pipe free.
+__device__ __forceinline__ void e4m3x4_to_bf16x2_raw(uint32_t w, uint32_t k16,
+						     uint32_t k2p28, uint32_t &lo,
+						     uint32_t &hi)
+{
+	const uint32_t l = (w & 0x0F0F0F0Fu) * k16;
+	const uint32_t h = __umulhi(w & 0x70707070u, k2p28) | (w & 0x80808080u);
+	lo = __byte_perm(l, h, 0x5140u);
+	hi = __byte_perm(l, h, 0x7362u);
+}
+
 // bf16 bits of e4m3(code) * 2^112 (the pre-biased scale), duplicated into
 // both halves of a word.
 __device__ __forceinline__ uint32_t mx_scale_lut_entry(uint32_t code)

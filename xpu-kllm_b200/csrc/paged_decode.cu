@@ -40,11 +40,19 @@
 namespace kllm {
 namespace {
 
+#ifndef KLLM_DEC_STAGES
+#define KLLM_DEC_STAGES 2       // bulk-copy ring depth per warp
+#endif
+#ifndef KLLM_DEC_MIN_CTAS_MX
+#define KLLM_DEC_MIN_CTAS_MX 4  // resident MX decode CTAs per SM (register cap)
+#endif
+
 constexpr int kTile = 16;
 constexpr int kWarps = KLLM_DEC_WARPS;
 constexpr int kSlotO = 0;                       // o[8][128]
 constexpr int kSlotM = KLLM_MAX_GROUP * 128;    // m[8]
 constexpr int kSlotL = kSlotM + KLLM_MAX_GROUP; // l[8]
+constexpr float kLazyLog2 = 8.f;                // reference max slack (p <= 256)
 
 template <int D, int KVT>
 struct Geom {
@@ -53,8 +61,8 @@ struct Geom {
 	static constexpr int SCL = MX ? kTile * D / 8 : 0;          // scales / tile
 	static constexpr int KV = PAY + SCL;                        // one of K, V
 	static constexpr int STAGE = 2 * KV;
-	static constexpr int NST = 3;                               // ring depth
-	static constexpr int MIN_CTAS = MX ? 4 : 2;                 // per SM (16 / 8 warps)
+	static constexpr int NST = KLLM_DEC_STAGES;                 // ring depth
+	static constexpr int MIN_CTAS = MX ? KLLM_DEC_MIN_CTAS_MX : 2;  // per SM
 };
 
 struct DevEntry {  // userspace/gpu/paged_attention.cu:18-22 (24 bytes)
@@ -80,7 +88,7 @@ struct SmemLayout {
 		bar = align_up((size_t)stage_bytes * nst * kWarps, 128);
 		meta = bar + sizeof(uint64_t) * nst * kWarps;
 		lut = align_up(meta + sizeof(int) * nst * kWarps, 16);
-		prefix = lut + 256 * sizeof(uint32_t);
+		prefix = lut + 260 * sizeof(uint32_t);  // 256 scale entries + 4 constants
 		slen = prefix + sizeof(int) * (S + 1);
 		total = slen + sizeof(int) * S;
 	}
@@ -147,11 +155,13 @@ __device__ __forceinline__ void lds_words(uint32_t (&w)[N], const uint8_t *p)
 }
 
 // Block-table entries for 32 consecutive tiles of the warp's stream, one per
-// lane, plus the tile's kv head / sub-tile / valid-token count.
+// lane. load_batch issues the entry loads; finalize_batch (called 32 tiles
+// later, when the loads have long landed) turns them into the K/V head
+// section addresses of the tile, so issuing a copy costs only shuffles.
 struct Batch {
-	unsigned long long k, v;
+	unsigned long long k, v;  // raw entry, then section base addresses
 	int valid;
-	int pack;  // ntok | sub << 8 | h << 16
+	int pack;  // ntok | sub << 8 | h << 16; after finalize: ntok | sub << 8
 };
 
 __device__ __forceinline__ void load_batch(Batch &b, const kllm_decode_args &a,
@@ -176,6 +186,22 @@ __device__ __forceinline__ void load_batch(Batch &b, const kllm_decode_args &a,
 		b.valid = __ldg(&e->valid);
 		b.pack = ntok | (sub << 8) | (c.h << 16);
 	}
+}
+
+// Raw entry -> section addresses; pack keeps ntok (0: nothing to copy) and sub.
+__device__ __forceinline__ void finalize_batch(Batch &b, const kllm_decode_args &a,
+					       size_t sec)
+{
+	const int ntok = b.pack & 0xFF, sub = (b.pack >> 8) & 0xFF, h = b.pack >> 16;
+	const bool present = b.valid && b.k != 0ull;
+	const bool aligned = ((b.k | b.v) & 15ull) == 0ull;
+	if (present && !aligned && a.err)
+		atomicOr(a.err, 0x2u);
+	const bool ok = present && aligned && ntok > 0;
+	const unsigned long long off = a.layer_off + (unsigned long long)h * sec;
+	b.k += off;
+	b.v += off;
+	b.pack = (ok ? ntok : 0) | (sub << 8);
 }
 
 template <int D>
@@ -208,7 +234,8 @@ template <int D, int KVT>
 __device__ __forceinline__ void tile_compute(
     const uint8_t *sK, const uint8_t *sV, const uint32_t *lut, int ntok,
     const uint32_t (&q)[D / 8], float (&o)[D / 16][4], float &m0, float &m1,
-    float &l0, float &l1, float scale_log2, int lane)
+    float &l0, float &l1, float &mx0, float &mx1, float scale_log2, int lane,
+    uint32_t k16, uint32_t k2p28)
 {
 	using Gm = Geom<D, KVT>;
 	const int g = lane >> 2, c = lane & 3;
@@ -229,14 +256,21 @@ __device__ __forceinline__ void tile_compute(
 			sw0 = *reinterpret_cast<const uint16_t *>(sK + kTile * D + g * 8 + c * 2);
 			sw1 = *reinterpret_cast<const uint16_t *>(sK + kTile * D + (g + 8) * 8 + c * 2);
 		}
+		uint32_t sc0[D / 32], sc1[D / 32];
+#pragma unroll
+		for (int b = 0; b < D / 32; ++b) {
+			sc0[b] = lut[__byte_perm(sw0, 0u, 0x4440u | b)];
+			sc1[b] = lut[__byte_perm(sw1, 0u, 0x4440u | b)];
+		}
 #pragma unroll
 		for (int j = 0; j < D / 16; ++j) {
-			const uint32_t sc0 = lut[(sw0 >> (8 * (j >> 1))) & 0xFFu];
-			const uint32_t sc1 = lut[(sw1 >> (8 * (j >> 1))) & 0xFFu];
-			const uint32_t a0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k0[j], false), sc0);
-			const uint32_t a2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k0[j], true), sc0);
-			const uint32_t a1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], false), sc1);
-			const uint32_t a3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(k1[j], true), sc1);
+			uint32_t r0lo, r0hi, r1lo, r1hi;
+			e4m3x4_to_bf16x2_raw(k0[j], k16, k2p28, r0lo, r0hi);
+			e4m3x4_to_bf16x2_raw(k1[j], k16, k2p28, r1lo, r1hi);
+			const uint32_t a0 = bf16x2_mul(r0lo, sc0[j >> 1]);
+			const uint32_t a2 = bf16x2_mul(r0hi, sc0[j >> 1]);
+			const uint32_t a1 = bf16x2_mul(r1lo, sc1[j >> 1]);
+			const uint32_t a3 = bf16x2_mul(r1hi, sc1[j >> 1]);
 			if (j & 1)
 				mma_bf16(s2, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
 			else
@@ -261,33 +295,43 @@ __device__ __forceinline__ void tile_compute(
 	for (int i = 0; i < 4; ++i)
 		s[i] += s2[i];
 
-	// ---- online softmax (log2 domain) ----------------------------------------
+	// ---- online softmax (log2 domain, lazy reference max) ---------------------
+	// m0/m1 are warp-uniform reference maxima per head. They are raised only
+	// when some lane's score exceeds them by more than kLazyLog2, so most tiles
+	// skip the cross-lane max and the O rescale; p then stays <= 2^kLazyLog2.
+	// mx0/mx1 track each lane's exact running maximum for the final triple.
 	const bool v0 = g < ntok, v1 = g + 8 < ntok;
 	const float x0 = v0 ? s[0] * scale_log2 : -CUDART_INF_F;  // tok g,   head 2c
 	const float x1 = v0 ? s[1] * scale_log2 : -CUDART_INF_F;  // tok g,   head 2c+1
 	const float x2 = v1 ? s[2] * scale_log2 : -CUDART_INF_F;  // tok g+8, head 2c
 	const float x3 = v1 ? s[3] * scale_log2 : -CUDART_INF_F;  // tok g+8, head 2c+1
 	float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+	mx0 = fmaxf(mx0, t0);
+	mx1 = fmaxf(mx1, t1);
+	if (__any_sync(0xffffffffu, t0 > m0 + kLazyLog2 || t1 > m1 + kLazyLog2)) {
 #pragma unroll
-	for (int off = 4; off < 32; off <<= 1) {
-		t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
-		t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
-	}
-	const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);  // finite: ntok >= 1
-	const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-	const float p0 = exp2f(x0 - mn0), p2 = exp2f(x2 - mn0);
-	const float p1 = exp2f(x1 - mn1), p3 = exp2f(x3 - mn1);
-	l0 = l0 * al0 + (p0 + p2);
-	l1 = l1 * al1 + (p1 + p3);
-	m0 = mn0;
-	m1 = mn1;
+		for (int off = 4; off < 32; off <<= 1) {
+			t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+			t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+		}
+		const float mn0 = fmaxf(m0, t0), mn1 = fmaxf(m1, t1);  // finite: ntok >= 1
+		const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+		l0 *= al0;
+		l1 *= al1;
+		m0 = mn0;
+		m1 = mn1;
 #pragma unroll
-	for (int mt = 0; mt < D / 16; ++mt) {
-		o[mt][0] *= al0;
-		o[mt][1] *= al1;
-		o[mt][2] *= al0;
-		o[mt][3] *= al1;
+		for (int mt = 0; mt < D / 16; ++mt) {
+			o[mt][0] *= al0;
+			o[mt][1] *= al1;
+			o[mt][2] *= al0;
+			o[mt][3] *= al1;
+		}
 	}
+	const float p0 = exp2f(x0 - m0), p2 = exp2f(x2 - m0);
+	const float p1 = exp2f(x1 - m1), p3 = exp2f(x3 - m1);
+	l0 += p0 + p2;
+	l1 += p1 + p3;
 	// P as bf16 hi + bf16 lo (16 significant bits): a bf16-only P misses the
 	// 1e-3 absolute bound on outputs built from large, cancelling V values.
 	const uint32_t h01 = pack_bf16x2(p0, p1), h23 = pack_bf16x2(p2, p3);
@@ -336,16 +380,21 @@ __device__ __forceinline__ void tile_compute(
 			const uint32_t c01b = __byte_perm(w0[i], w1[i], 0x7362u);
 			const uint32_t c23a = __byte_perm(w2[i], w3[i], 0x5140u);
 			const uint32_t c23b = __byte_perm(w2[i], w3[i], 0x7362u);
-			const uint32_t e0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, false), s01[bb]);
-			const uint32_t e1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01a, true), s01[bb]);
-			const uint32_t e2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, false), s23[bb]);
-			const uint32_t e3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23a, true), s23[bb]);
+			uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
+			e4m3x4_to_bf16x2_raw(c01a, k16, k2p28, x0, x1);  // (R0,R1) bytes 0 | 1
+			e4m3x4_to_bf16x2_raw(c23a, k16, k2p28, x2, x3);
+			e4m3x4_to_bf16x2_raw(c01b, k16, k2p28, y0, y1);  // (R0,R1) bytes 2 | 3
+			e4m3x4_to_bf16x2_raw(c23b, k16, k2p28, y2, y3);
+			const uint32_t e0 = bf16x2_mul(x0, s01[bb]);
+			const uint32_t e1 = bf16x2_mul(x1, s01[bb]);
+			const uint32_t e2 = bf16x2_mul(x2, s23[bb]);
+			const uint32_t e3 = bf16x2_mul(x3, s23[bb]);
 			mma_bf16(o[2 * i], e0, e1, e2, e3, b0, b1);
 			mma_bf16(o[2 * i], e0, e1, e2, e3, c0, c1);
-			const uint32_t f0 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, false), s01[bb]);
-			const uint32_t f1 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c01b, true), s01[bb]);
-			const uint32_t f2 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, false), s23[bb]);
-			const uint32_t f3 = bf16x2_mul(e4m3x2_to_bf16x2_raw(c23b, true), s23[bb]);
+			const uint32_t f0 = bf16x2_mul(y0, s01[bb]);
+			const uint32_t f1 = bf16x2_mul(y1, s01[bb]);
+			const uint32_t f2 = bf16x2_mul(y2, s23[bb]);
+			const uint32_t f3 = bf16x2_mul(y3, s23[bb]);
 			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, b0, b1);
 			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, c0, c1);
 		}
@@ -525,6 +574,10 @@ decode_kernel(const kllm_decode_args a)
 	if constexpr (Gm::MX)
 		for (int i = tid; i < 256; i += blockDim.x)
 			lut[i] = mx_scale_lut_entry((uint32_t)i);
+	if (tid == 0) {
+		lut[256] = 16u;        // multiplier constants for the dequant, read
+		lut[257] = 1u << 28;   // back at run time (kept out of immediates)
+	}
 	{
 		bool too_long = false;
 		const int cap = a.max_blocks * a.block_size;
@@ -604,38 +657,32 @@ decode_kernel(const kllm_decode_args a)
 	Batch cur, nxt;
 	load_batch(cur, a, prefix, slen, xa, n, 0, lane, tpp);
 	load_batch(nxt, a, prefix, slen, xa, n, 32, lane, tpp);
+	finalize_batch(cur, a, sec);
 	int pb = 0;
 
 	auto issue = [&](int pos) {
 		int bi = pos - pb;
 		if (bi >= 32) {
 			cur = nxt;
+			finalize_batch(cur, a, sec);
 			pb += 32;
 			bi -= 32;
 			load_batch(nxt, a, prefix, slen, xa, n, pb + 32, lane, tpp);
 		}
 		const unsigned long long ek = __shfl_sync(0xffffffffu, cur.k, bi);
 		const unsigned long long ev = __shfl_sync(0xffffffffu, cur.v, bi);
-		const int valid = __shfl_sync(0xffffffffu, cur.valid, bi);
 		const int pack = __shfl_sync(0xffffffffu, cur.pack, bi);
 		if (lane == 0) {
 			const int st = pos % Gm::NST;
-			const int ntok = pack & 0xFF, sub = (pack >> 8) & 0xFF, h = pack >> 16;
-			const bool present = valid && ek != 0ull;
-			const bool aligned = ((ek | ev) & 15ull) == 0ull;
-			if (present && !aligned && a.err)
-				atomicOr(a.err, 0x2u);
-			const bool ok = present && aligned && ntok > 0;
-			wmeta[st] = ok ? ntok : 0;
+			const int ntok = pack & 0xFF, sub = pack >> 8;
+			wmeta[st] = ntok;
 			uint64_t *bar = &wbar[st];
-			if (ok) {
+			if (ntok) {
 				mbar_arrive_expect_tx(bar, Gm::STAGE);
 				uint8_t *dK = wst + (size_t)st * Gm::STAGE;
 				uint8_t *dV = dK + Gm::KV;
-				const uint8_t *sK = reinterpret_cast<const uint8_t *>(ek) +
-						    a.layer_off + (size_t)h * sec;
-				const uint8_t *sV = reinterpret_cast<const uint8_t *>(ev) +
-						    a.layer_off + (size_t)h * sec;
+				const uint8_t *sK = reinterpret_cast<const uint8_t *>(ek);
+				const uint8_t *sV = reinterpret_cast<const uint8_t *>(ev);
 				if (Gm::MX && tpp == 1) {  // payload + scales contiguous
 					bulk_g2s_stream(dK, sK, Gm::KV, bar, policy);
 					bulk_g2s_stream(dV, sV, Gm::KV, bar, policy);
@@ -669,7 +716,9 @@ decode_kernel(const kllm_decode_args a)
 	for (int mt = 0; mt < D / 16; ++mt)
 		o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 	float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+	float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
 	const int g = lane >> 2, c = lane & 3;
+	const uint32_t k16 = lut[256], k2p28 = lut[257];
 
 	for (int i = 0; i < n; ++i) {
 		if (p < n) {
@@ -686,7 +735,8 @@ decode_kernel(const kllm_decode_args a)
 		if (ntok > 0) {
 			const uint8_t *sK = wst + (size_t)st * Gm::STAGE;
 			tile_compute<D, KVT>(sK, sK + Gm::KV, lut, ntok, q, o, m0,
-					     m1, l0, l1, a.scale_log2, lane);
+					     m1, l0, l1, mx0, mx1, a.scale_log2, lane, k16,
+					     k2p28);
 		}
 		__syncwarp();
 
@@ -698,6 +748,27 @@ decode_kernel(const kllm_decode_args a)
 		}
 
 		// ---- piece finished: normalise, or publish a partial -------------
+		// Re-reference l and O from the lazy maximum to the exact one.
+#pragma unroll
+		for (int off = 4; off < 32; off <<= 1) {
+			mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+			mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+		}
+		{
+			const float f0 = mx0 > m0 ? exp2f(m0 - mx0) : 1.f;
+			const float f1 = mx1 > m1 ? exp2f(m1 - mx1) : 1.f;
+			if (mx0 > m0) m0 = mx0;
+			if (mx1 > m1) m1 = mx1;
+			l0 *= f0;
+			l1 *= f1;
+#pragma unroll
+			for (int mt = 0; mt < D / 16; ++mt) {
+				o[mt][0] *= f0;
+				o[mt][1] *= f1;
+				o[mt][2] *= f0;
+				o[mt][3] *= f1;
+			}
+		}
 		float L0 = l0, L1 = l1;
 #pragma unroll
 		for (int off = 4; off < 32; off <<= 1) {
@@ -776,6 +847,7 @@ decode_kernel(const kllm_decode_args a)
 		for (int mt = 0; mt < D / 16; ++mt)
 			o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 		m0 = m1 = -CUDART_INF_F;
+		mx0 = mx1 = -CUDART_INF_F;
 		l0 = l1 = 0.f;
 	}
 }
