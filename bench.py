@@ -34,6 +34,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "xpu-kllm_b200"))
 
+from kllm_b200 import multigpu as mg  # noqa: E402
 from kllm_b200 import workloads as wl  # noqa: E402
 
 METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200"
@@ -46,17 +47,6 @@ def peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
-
-
-def lpt_shard(lens: np.ndarray, n: int) -> list[list[int]]:
-    """Longest-processing-time packing of requests onto n ranks."""
-    loads = [0] * n
-    out: list[list[int]] = [[] for _ in range(n)]
-    for s in np.argsort(-lens, kind="stable"):
-        r = int(np.argmin(loads))
-        out[r].append(int(s))
-        loads[r] += int(lens[s])
-    return [sorted(x) for x in out]
 
 
 class Clocks:
@@ -115,7 +105,7 @@ class DecodeRig:
                  torch, device: int, seed: int = 0, arena_factor: float = 1.25):
         self.cfg, self.be, self.torch = cfg, be, torch
         self.seqs = seqs
-        self.lens = all_lens[seqs].astype(np.int32)
+        self.lens = np.asarray(all_lens)[seqs].astype(np.int32)
         c = cfg
         self.B = len(seqs)
         dev = torch.device("cuda", device)
@@ -169,17 +159,50 @@ class DecodeRig:
                 assert rc == 0, f"append failed: {rc}"
         torch.cuda.synchronize()
 
+    split_kv = False
+
+    def enable_split_kv(self, rank: int, world: int, dist) -> None:
+        """Cross-GPU split-KV: partial triples per rank, merged over NCCL by
+        the library (kllm_gpu_comm_merge) inside every step."""
+        import ctypes
+        torch, c = self.torch, self.cfg
+        uid = (ctypes.c_uint8 * 128)()
+        if rank == 0:
+            rc = self.be.lib.kllm_gpu_comm_get_unique_id(uid)
+            assert rc == 0, f"comm id: {rc}"
+        t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
+        dist.broadcast(t, 0)
+        uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
+        rc = self.be.lib.kllm_gpu_comm_init(self.be.ctx, world, rank, uid, 120000)
+        if rc != 0:
+            raise RuntimeError(f"kllm_gpu_comm_init: {rc}")
+        rows = self.B * c.hq
+        self.pm = torch.empty((rows,), dtype=torch.float32, device="cuda")
+        self.pl = torch.empty_like(self.pm)
+        self.po = torch.empty((rows, c.d), dtype=torch.float32, device="cuda")
+        self.split_kv = True
+
     def launch(self, layer: int, stream: int, q_ptr=None, out_ptr=None) -> None:
         c = self.cfg
-        rc = self.be.decode_v2(
+        kw = dict(
             output=out_ptr or self.out[layer].data_ptr(),
             query=q_ptr or self.q[layer].data_ptr(),
             block_tables=self.table.data_ptr(), seq_lens=self.seq_lens.data_ptr(),
             num_seqs=self.B, num_heads=c.hq, num_kv_heads=c.hkv, head_dim=c.d,
             max_blocks_per_seq=self.plan.max_blocks, block_size=c.block, kv_dtype=c.kv_dtype,
             layer=layer, layer_stride=c.layer_stride(), scale=c.scale, split=1, stream=stream)
+        if self.split_kv:
+            kw.update(output=None, partial_m=self.pm.data_ptr(), partial_l=self.pl.data_ptr(),
+                      partial_o=self.po.data_ptr())
+        rc = self.be.decode_v2(**kw)
         if rc != 0:
             raise RuntimeError(f"decode launch failed: {rc}")
+        if self.split_kv:
+            rc = self.be.lib.kllm_gpu_comm_merge(
+                self.be.ctx, self.pm.data_ptr(), self.pl.data_ptr(), self.po.data_ptr(),
+                self.B * c.hq, c.d, out_ptr or self.out[layer].data_ptr(), stream, 0)
+            if rc != 0:
+                raise RuntimeError(f"kllm_gpu_comm_merge failed: {rc}")
 
     def step_bytes(self) -> int:
         return wl.algorithmic_bytes(self.cfg, self.lens)
@@ -240,11 +263,21 @@ def run_kllm(args) -> None:
     if args.layers:
         cfg = __import__("dataclasses").replace(cfg, layers=args.layers)
     lens_all = wl.context_lengths(cfg, args.seed)
-    shards = lpt_shard(lens_all, world)
-    mine = shards[rank]
-    rig = DecodeRig(cfg, mine, lens_all, be, torch, local, args.seed)
+    split_kv = cfg.batch == 1 and world > 1
+    if split_kv:
+        # one long context: this rank owns a contiguous range of its pages
+        pages = int((lens_all[0] + cfg.block - 1) // cfg.block)
+        lo, hi = mg.page_ranges(pages, world)[rank]
+        local_len = int(np.clip(lens_all[0] - lo * cfg.block, 0, (hi - lo) * cfg.block))
+        mine, lens_rank = [0], np.array([local_len], np.int32)
+    else:
+        mine = mg.lpt_shard(lens_all, world)[rank]
+        lens_rank = lens_all
+    rig = DecodeRig(cfg, mine, lens_rank, be, torch, local, args.seed)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
+    if split_kv:
+        rig.enable_split_kv(rank, world, dist)
 
     def barrier():
         if world > 1:
@@ -323,7 +356,7 @@ def run_kllm(args) -> None:
     t_ms = float(allst[:, 0].max())
     te_ms = float(allst[:, 1].max())
     total_bytes = float(allst[:, 2].sum())
-    total_tokens = float(allst[:, 3].sum())
+    total_tokens = float(cfg.batch) if split_kv else float(allst[:, 3].sum())
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -352,7 +385,9 @@ def run_kllm(args) -> None:
                        "kv_gb_per_step": round(total_bytes / 1e9, 3),
                        "arena_gb_rank0": round(float(allst[0, 5]) / 1e9, 2),
                        "l2": "inputs larger than L2 (KV per step >> 126 MB)",
-                       "parallelism": f"request-sharded x{world} (LPT), no collective"},
+                       "parallelism": (f"split-KV x{world} (page ranges) + NCCL all-gather "
+                                       f"merge" if split_kv else
+                                       f"request-sharded x{world} (LPT), no collective")},
             "tokens_per_s": round(total_tokens * args.steps / (t_ms * 1e-3), 1),
             "hbm_frac_8tbs": round(value / world / 8000.0, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,

@@ -186,7 +186,9 @@ struct kllm_gpu_attention_params_v2 {
 	float *partial_l;
 	float *partial_o;
 	uint32_t *err_word;          /* optional; KLLM_ERR_* bits are OR-ed in */
-	void *workspace;             /* optional; NULL = the context's workspace */
+	void *workspace;             /* optional; NULL = the context's workspace. A
+	                                caller workspace is zero-filled once before
+	                                its first use; calls leave it reusable */
 	uint64_t workspace_size;
 	void *stream;
 };

@@ -97,10 +97,13 @@ def _pages_from_rows(cfg, rows_pay, rows_sc, n_pages, tail_fill):
 
 
 def build_case(cfg: wl.DecodeConfig, seed: int = 0, seq_lens=None, batch=None,
-               invalid=None, tail_fill: int = 0xFF, max_blocks=None, layers=None) -> HostCase:
+               invalid=None, tail_fill: int = 0xFF, max_blocks=None, layers=None,
+               seq_ids=None) -> HostCase:
     """Seeded host case. ``invalid``: list of (seq, block) entries to mark invalid.
     ``tail_fill``: byte written past each sequence's last token (0xFF -> bf16 NaN,
-    so masking of the partial last page is exercised)."""
+    so masking of the partial last page is exercised). ``seq_ids``: global
+    request ids whose K/V streams the sequences use (default 0..batch-1), so a
+    shard of a batch holds the same data as the whole batch."""
     if batch is not None:
         cfg = replace(cfg, batch=batch)
     if layers is not None:
@@ -114,14 +117,15 @@ def build_case(cfg: wl.DecodeConfig, seed: int = 0, seq_lens=None, batch=None,
                          max(cfg.arena_slots, int(((np.maximum(seq_lens, 0) + cfg.block - 1)
                                                    // cfg.block).sum())))
     arena = np.zeros((plan.n_slots, cfg.slot_bytes()), dtype=np.uint8)
-    mult = wl.magnitudes(cfg, seed)
+    ids = list(range(len(seq_lens))) if seq_ids is None else [int(x) for x in seq_ids]
+    mult = wl.magnitudes(replace(cfg, batch=max(ids) + 1), seed)
     for layer in range(cfg.layers):
         loff = layer * cfg.layer_stride()
         for s, L in enumerate(seq_lens):
             if L <= 0:
                 continue
             n_pages = (int(L) + cfg.block - 1) // cfg.block
-            k, v = wl.seq_kv_bf16(cfg, s, int(L), seed, layer, mult)
+            k, v = wl.seq_kv_bf16(cfg, ids[s], int(L), seed, layer, mult)
             for which, x in ((0, k), (1, v)):
                 if cfg.kv_dtype == wl.KV_MX_FP8:
                     pay, sc = oracle.mx_quantize(x)

@@ -237,3 +237,28 @@ def test_rejects_bad_shapes(be):
     assert be.decode_v2(**dc.decode_kwargs(kv_dtype=7)) == kb.ENOSYS
     assert be.decode_v2(**dc.decode_kwargs(layer_stride=8)) == kb.EINVAL
     assert be.decode_v2(**dc.decode_kwargs(layer=-1)) == kb.EINVAL
+
+
+def test_c4_long_context_wide_merge(be):
+    """C4 at full size: one 131072-token context, 64 q / 8 kv heads. Every kv
+    head is split over hundreds of warps, so the partials go through the
+    queued wide merge; bf16 output and partial triples against the oracle."""
+    import torch
+    hc = kvcase.build_case(wl.C4)
+    dc = kvcase.DeviceCase(hc)
+    ref = hc.oracle_decode()
+    kvcase.assert_close_bf16(run_v2(be, dc), ref, what="C4")
+    c = hc.cfg
+    pm = torch.empty((1, c.hq), dtype=torch.float32, device="cuda")
+    pl = torch.empty_like(pm)
+    po = torch.empty((1, c.hq, c.d), dtype=torch.float32, device="cuda")
+    rc = be.decode_v2(**dc.decode_kwargs(output=None, partial_m=pm.data_ptr(),
+                                         partial_l=pl.data_ptr(), partial_o=po.data_ptr()))
+    assert rc == 0
+    torch.cuda.synchronize()
+    m, l, o = hc.oracle_partials()
+    kvcase.assert_close_f32(pm.cpu().numpy(), m, atol=2e-3, rtol=1e-3, what="m")
+    kvcase.assert_close_f32(pl.cpu().numpy(), l, atol=1e-2, rtol=1e-2, what="l")
+    kvcase.assert_close_f32(po.cpu().numpy(), o, what="o")
+    # a second call finds the merge queue empty again
+    kvcase.assert_close_bf16(run_v2(be, dc), ref, what="C4 again")

@@ -14,8 +14,9 @@
 //
 // Scratch: kScratchBytes (16 MiB) of file-scope device memory per device,
 // held until the process exits: arrival counters for up to kMaxSegments
-// (seq, kv head) pairs, then split-KV partial slots. The grid is cut to the
-// number of partial slots that fit. Every call reuses the same array, so
+// (seq, kv head) pairs, split-KV partial slots, and the queue of long
+// segments for the wide merge. The grid is cut to the number of partial
+// slots that fit. Every call reuses the same array, so
 // calls whose kernels overlap on the GPU (different streams, or different
 // host threads) race on it and must be serialised by the caller.
 
@@ -32,7 +33,8 @@ constexpr size_t kScratchBytes = 16u << 20;          // 16 MiB per device
 constexpr int kMaxSegments = 65536;                  // num_seqs * num_kv_heads
 constexpr size_t kCounterBytes = sizeof(unsigned) * kMaxSegments;  // 256 KiB
 constexpr size_t kSlotBytes = 2ull * KLLM_SLOT_FLOATS * sizeof(float);  // per warp
-constexpr int kMaxWarps = (int)((kScratchBytes - kCounterBytes) / kSlotBytes);
+constexpr size_t kListOffset = kScratchBytes - KLLM_MERGE_LIST_BYTES;  // merge queue
+constexpr int kMaxWarps = (int)((kListOffset - kCounterBytes) / kSlotBytes);
 constexpr int kMaxDevices = 64;
 
 // The scratch itself. Host code must not use this name as an address: on
@@ -114,7 +116,9 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	// The counters must start at zero; the array keeps whatever the last call
 	// left, so clear the words this call uses (no allocation involved).
 	const size_t segs = (size_t)p->num_seqs * p->num_kv_heads;
-	if (cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess) {
+	void *list = scratch + kListOffset;
+	if (cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess ||
+	    cudaMemsetAsync(list, 0, 32, st) != cudaSuccess) {
 		(void)cudaGetLastError();
 		return KLLM_EIO;
 	}
@@ -142,6 +146,7 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	a.split = 1;
 	a.ws_part = part;
 	a.ws_cnt = cnt;
+	a.ws_list = list;
 
 	const size_t row = (size_t)p->num_heads * p->head_dim;
 	for (int s0 = 0; s0 < p->num_seqs; s0 += KLLM_MAX_SEQS_LAUNCH) {
@@ -168,7 +173,8 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 		if (grid * KLLM_DEC_WARPS > kMaxWarps)
 			grid = kMaxWarps / KLLM_DEC_WARPS;
 		c.total_warps = grid * KLLM_DEC_WARPS;
-		if (kllm_decode_launch(&c, grid, st) != 0) {
+		if (kllm_decode_launch(&c, grid, st) != 0 ||
+		    kllm_decode_merge_launch(&c, sms, st) != 0) {
 			(void)cudaGetLastError();
 			return KLLM_EIO;
 		}

@@ -40,8 +40,21 @@ struct kllm_decode_args {
 	int split;                /* 1: tile-balanced split-KV; 0: one warp per segment */
 	float *ws_part;           /* split: partial slots [warps][2][KLLM_SLOT_FLOATS] */
 	unsigned *ws_cnt;         /* split: arrival counters [S*Hkv], zero between calls */
+	void *ws_list;            /* split: merge work list (KLLM_MERGE_LIST_BYTES, header
+	                             zero between calls) or NULL: merge in the decode */
 	int total_warps;          /* warps launched (grid * KLLM_DEC_WARPS) */
 };
+
+/* Segments split over more than KLLM_FUSED_MERGE_MAX warps are not merged by
+ * the last warp of the decode but queued for kllm_decode_merge_launch, which
+ * merges each (segment, query head) with a whole CTA. */
+#define KLLM_FUSED_MERGE_MAX   16
+#define KLLM_MERGE_LIST_CAP    1024
+#define KLLM_MERGE_LIST_BYTES  (32 + 24 * KLLM_MERGE_LIST_CAP)
+
+/* Merges the queued segments of the decode launched with `a` (same args). */
+int kllm_decode_merge_launch(const struct kllm_decode_args *a, int num_sms,
+			     void *stream);
 
 /* Dynamic shared memory of one decode CTA for this shape. */
 size_t kllm_decode_smem_bytes(int head_dim, int kv_dtype, int num_seqs);

@@ -150,12 +150,18 @@ struct kllm_gpu_ctx *kllm_gpu_create(void)
 	if (ctas <= 0)
 		goto fail_stream;
 	ctx->ws_max_warps = ctx->num_sms * ctas * KLLM_DEC_WARPS;
-	ctx->ws_part_bytes = (uint64_t)ctx->ws_max_warps * 2 * KLLM_SLOT_FLOATS * sizeof(float);
+	ctx->ws_part_bytes = (uint64_t)ctx->ws_max_warps * 2 * KLLM_SLOT_FLOATS * sizeof(float) +
+			     KLLM_MERGE_LIST_BYTES;
 	if (cudaMalloc((void **)&ctx->ws_part, ctx->ws_part_bytes) != cudaSuccess)
 		goto fail_stream;
 	if (cudaMalloc((void **)&ctx->ws_cnt, sizeof(unsigned) * KLLM_CNT_CAP) != cudaSuccess)
 		goto fail_ws;
 	if (cudaMemset(ctx->ws_cnt, 0, sizeof(unsigned) * KLLM_CNT_CAP) != cudaSuccess)
+		goto fail_cnt;
+	/* the merge list lives at the end of the partial region; its header
+	 * must start at zero (the kernels leave it at zero after each call) */
+	if (cudaMemset((uint8_t *)ctx->ws_part + ctx->ws_part_bytes - KLLM_MERGE_LIST_BYTES,
+		       0, KLLM_MERGE_LIST_BYTES) != cudaSuccess)
 		goto fail_cnt;
 	if (cudaDeviceSynchronize() != cudaSuccess)
 		goto fail_cnt;
@@ -380,7 +386,7 @@ static int check_decode_shape(int num_seqs, int num_heads, int num_kv_heads,
 
 /* Launches one decode over sequences [s0, s0+ns) of the batch. */
 static int decode_chunk(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *a,
-			int split, float *ws_part, unsigned *ws_cnt,
+			int split, float *ws_part, unsigned *ws_cnt, void *ws_list,
 			int max_warps, int num_sms, cudaStream_t st)
 {
 	int ctas = decode_ctas(ctx, a->head_dim, a->kv_dtype, a->num_seqs);
@@ -394,12 +400,19 @@ static int decode_chunk(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *a,
 	a->split = split;
 	a->ws_part = ws_part;
 	a->ws_cnt = ws_cnt;
+	a->ws_list = split ? ws_list : NULL;
 	a->total_warps = grid * KLLM_DEC_WARPS;
 	int e = kllm_decode_launch(a, grid, st);
 	if (e)
 		return KLLM_EIO;
 	if (ctx)
 		ctx->stats.launches++;
+	if (split && ws_list) {
+		if (kllm_decode_merge_launch(a, num_sms, st))
+			return KLLM_EIO;
+		if (ctx)
+			ctx->stats.launches++;
+	}
 	return KLLM_OK;
 }
 
@@ -418,6 +431,13 @@ static int decode_common(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *base
 			return KLLM_ENOSPC;
 		if ((uint64_t)per > by_cnt)
 			per = (int)by_cnt;
+	}
+	void *ws_list = NULL;
+	if (split) {
+		if (ws_part_bytes < KLLM_MERGE_LIST_BYTES)
+			return KLLM_ENOSPC;
+		ws_part_bytes -= KLLM_MERGE_LIST_BYTES;
+		ws_list = (uint8_t *)ws_part + ws_part_bytes;
 	}
 	int max_warps = (int)(ws_part_bytes / (2ull * KLLM_SLOT_FLOATS * sizeof(float)));
 	if (split && max_warps < KLLM_DEC_WARPS)
@@ -438,7 +458,7 @@ static int decode_common(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *base
 			a.pl = base->pl + (size_t)s0 * base->num_heads;
 			a.po = base->po + (size_t)s0 * row;
 		}
-		int rc = decode_chunk(ctx, &a, split, ws_part, ws_cnt, max_warps,
+		int rc = decode_chunk(ctx, &a, split, ws_part, ws_cnt, ws_list, max_warps,
 				      num_sms, st);
 		if (rc)
 			return rc;
@@ -567,8 +587,9 @@ int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
 	unsigned *cnt = ctx->ws_cnt;
 	uint64_t cnt_cap = KLLM_CNT_CAP;
 	if (split && p->workspace) {
-		/* caller workspace: counters first (zeroed by the caller once),
-		 * then the partial slots */
+		/* caller workspace: counters first, then the partial slots and
+		 * the merge list; the caller zeroes it once, the kernels leave it
+		 * ready for the next call */
 		uint64_t cnt_bytes = sizeof(unsigned) * (uint64_t)p->num_seqs * p->num_kv_heads;
 		cnt_bytes = (cnt_bytes + 255) & ~255ull;
 		if (p->workspace_size <= cnt_bytes)

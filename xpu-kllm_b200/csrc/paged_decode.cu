@@ -75,6 +75,18 @@ struct Seg {
 	int s, h, j, ts;  // seq, kv head, tile in segment, tiles in segment
 };
 
+// Merge work list (KLLM_MERGE_LIST_BYTES): header, then items.
+struct ListHeader {
+	unsigned count, done;
+	long long T, W;
+	long long pad;
+};
+struct ListItem {
+	int s, h, ts, pad;
+	long long seg_x0;
+};
+static_assert(sizeof(ListHeader) == 32 && sizeof(ListItem) == 24, "list layout");
+
 __host__ __device__ inline size_t align_up(size_t x, size_t a)
 {
 	return (x + a - 1) / a * a;
@@ -823,7 +835,27 @@ decode_kernel(const kllm_decode_args a)
 			old = __shfl_sync(0xffffffffu, old, 0);
 			if ((long long)old == npieces - 1) {
 				__threadfence();
-				merge_segment<D>(a, cc, seg_x0, T, W, unbias, lane);
+				bool fused = npieces <= KLLM_FUSED_MERGE_MAX || !a.ws_list;
+				if (!fused) {  // long segment: queue it for the wide merge
+					ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
+					ListItem *li = reinterpret_cast<ListItem *>(lh + 1);
+					unsigned idx = 0;
+					if (lane == 0) {
+						idx = atomicAdd(&lh->count, 1u);
+						if (idx < KLLM_MERGE_LIST_CAP) {
+							li[idx].s = cc.s;
+							li[idx].h = cc.h;
+							li[idx].ts = cc.ts;
+							li[idx].seg_x0 = seg_x0;
+							lh->T = T;
+							lh->W = W;
+						}
+					}
+					idx = __shfl_sync(0xffffffffu, idx, 0);
+					fused = idx >= KLLM_MERGE_LIST_CAP;
+				}
+				if (fused)
+					merge_segment<D>(a, cc, seg_x0, T, W, unbias, lane);
 				if (lane == 0)
 					*cnt = 0u;  // ready for the next launch
 			}
@@ -849,6 +881,99 @@ decode_kernel(const kllm_decode_args a)
 		m0 = m1 = -CUDART_INF_F;
 		mx0 = mx1 = -CUDART_INF_F;
 		l0 = l1 = 0.f;
+	}
+}
+
+// Wide merge of the queued long segments: one CTA of 8 warps per
+// (segment, query head); warp w folds pieces w, w+8, ... with the
+// log-sum-exp rule, the warps are combined in shared memory. The last CTA
+// to finish clears the list header for the next launch.
+template <int D>
+__global__ void __launch_bounds__(256)
+merge_big_kernel(const kllm_decode_args a, float unbias)
+{
+	__shared__ float sm_m[8], sm_l[8];
+	__shared__ float sm_o[8][D];
+	__shared__ int last;
+	ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
+	const ListItem *li = reinterpret_cast<const ListItem *>(lh + 1);
+	const unsigned count = min(*reinterpret_cast<volatile unsigned *>(&lh->count),
+				   (unsigned)KLLM_MERGE_LIST_CAP);
+	const long long T = lh->T, W = lh->W;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	constexpr int NV = D / 32;
+	const long long pairs = (long long)count * a.group;
+
+	for (long long pr = blockIdx.x; pr < pairs; pr += gridDim.x) {
+		const ListItem it = li[pr / a.group];
+		const int hh = (int)(pr % a.group);
+		const long long w0 = owner_warp(it.seg_x0, T, W);
+		const long long np = owner_warp(it.seg_x0 + it.ts - 1, T, W) - w0 + 1;
+		float M = -CUDART_INF_F, L = 0.f, acc[NV];
+#pragma unroll
+		for (int i = 0; i < NV; ++i)
+			acc[i] = 0.f;
+		for (long long r = warp; r < np; r += 8) {
+			const long long wr = w0 + r;
+			const int which = (r == 0 && wr * T / W != it.seg_x0) ? 1 : 0;
+			const float *slot = a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
+			const float lr = __ldcg(slot + kSlotL + hh);
+			if (!(lr > 0.f))
+				continue;
+			const float mr = __ldcg(slot + kSlotM + hh);
+			const float mn = fmaxf(M, mr);
+			const float fo = exp2f(M - mn), fr = exp2f(mr - mn);
+			L = L * fo + lr * fr;
+			M = mn;
+			const float *src = slot + kSlotO + hh * D + lane * NV;
+#pragma unroll
+			for (int i = 0; i < NV; ++i)
+				acc[i] = acc[i] * fo + __ldcg(src + i) * fr;
+		}
+		if (lane == 0) {
+			sm_m[warp] = M;
+			sm_l[warp] = L;
+		}
+#pragma unroll
+		for (int i = 0; i < NV; ++i)
+			sm_o[warp][lane * NV + i] = acc[i];
+		__syncthreads();
+		if (threadIdx.x < D) {
+			const int d = threadIdx.x;
+			float Mt = -CUDART_INF_F;
+			for (int w = 0; w < 8; ++w)
+				if (sm_l[w] > 0.f)
+					Mt = fmaxf(Mt, sm_m[w]);
+			float Lt = 0.f, o = 0.f;
+			for (int w = 0; w < 8; ++w)
+				if (sm_l[w] > 0.f) {
+					const float f = exp2f(sm_m[w] - Mt);
+					Lt += sm_l[w] * f;
+					o += sm_o[w][d] * f;
+				}
+			const size_t row = (size_t)it.s * a.num_heads + (size_t)it.h * a.group + hh;
+			const float inv = Lt > 0.f ? unbias / Lt : 0.f;
+			if (a.pm) {
+				a.po[row * D + d] = o * inv;
+				if (d == 0) {
+					a.pm[row] = Lt > 0.f ? Mt * 0.69314718055994531f : -CUDART_INF_F;
+					a.pl[row] = Lt;
+				}
+			} else {
+				__nv_bfloat16 b = __float2bfloat16_rn(o * inv);
+				reinterpret_cast<__nv_bfloat16 *>(a.out)[row * D + d] = b;
+			}
+		}
+		__syncthreads();
+	}
+	if (threadIdx.x == 0) {
+		__threadfence();
+		last = atomicAdd(&lh->done, 1u) == gridDim.x - 1;
+	}
+	__syncthreads();
+	if (last && threadIdx.x == 0) {
+		lh->count = 0u;
+		lh->done = 0u;
 	}
 }
 
@@ -909,6 +1034,23 @@ extern "C" int kllm_decode_ctas_per_sm(int head_dim, int kv_dtype, int num_seqs)
 		return kv_dtype ? Launcher<64, 1>::occupancy(num_seqs)
 				: Launcher<64, 0>::occupancy(num_seqs);
 	return 0;
+}
+
+extern "C" int kllm_decode_merge_launch(const struct kllm_decode_args *a,
+					int num_sms, void *stream)
+{
+	if (!a->ws_list || !a->split)
+		return 0;
+	cudaStream_t st = static_cast<cudaStream_t>(stream);
+	const float unbias = a->kv_dtype ? kMxUnbias : 1.f;
+	const int grid = num_sms > 0 ? num_sms : 148;
+	if (a->head_dim == 128)
+		merge_big_kernel<128><<<grid, 256, 0, st>>>(*a, unbias);
+	else if (a->head_dim == 64)
+		merge_big_kernel<64><<<grid, 256, 0, st>>>(*a, unbias);
+	else
+		return (int)cudaErrorInvalidValue;
+	return (int)cudaGetLastError();
 }
 
 extern "C" int kllm_decode_launch(const struct kllm_decode_args *a, int grid,
