@@ -281,6 +281,48 @@ struct kllm_gpu_gather_params {
 int kllm_gpu_gather_debug(struct kllm_gpu_ctx *ctx,
 			  const struct kllm_gpu_gather_params *p);
 
+/* Chunked prefill (no counterpart in the reference GPU path, which has no
+ * prefill; the math is userspace/compute/ace_attention.c:85-134 per query row
+ * with keys [0, position]). The chunks of num_seqs sequences are packed
+ * token-major: sequence s owns rows cu_seqlens[s] .. cu_seqlens[s+1]-1 of
+ * q/k/v/output. Query j of sequence s sits at position ctx_lens[s] + j and
+ * attends to the sequence's first ctx_lens[s] tokens, read from the paged
+ * cache through the block table (pages of block_size tokens, kv_dtype BF16
+ * or MX-FP8, invalid pages skipped), and to chunk keys 0..j (causal).
+ * head_dim 128; num_heads / num_kv_heads in {1, 2, 4, 8}. max_chunk bounds
+ * every chunk length (it sizes the grid). append = 1 also writes the chunk's
+ * K/V into the cache at positions ctx_lens[s] + j (quantize-on-write, as
+ * kllm_gpu_kv_append_v2). Runs on the tcgen05 tensor cores. */
+struct kllm_gpu_prefill_params {
+	uint32_t struct_size;
+	uint32_t flags;
+	void *output;                /* bf16 [num_tokens][num_heads][head_dim] */
+	const void *q;               /* bf16 [num_tokens][num_heads][head_dim] */
+	const void *k;               /* bf16 [num_tokens][num_kv_heads][head_dim] */
+	const void *v;               /* bf16 [num_tokens][num_kv_heads][head_dim] */
+	const int *cu_seqlens;       /* int32 [num_seqs + 1], cu_seqlens[0] = 0 */
+	const int *ctx_lens;         /* int32 [num_seqs] */
+	int num_seqs;
+	int num_tokens;              /* cu_seqlens[num_seqs] */
+	int max_chunk;
+	int num_heads;
+	int num_kv_heads;
+	int head_dim;
+	const void *block_tables;    /* kllm_block_table_entry [num_seqs][max_blocks_per_seq] */
+	int max_blocks_per_seq;
+	int block_size;
+	int kv_dtype;
+	int layer;
+	uint64_t layer_stride;
+	float scale;
+	int append;
+	uint32_t *err_word;
+	void *stream;
+};
+
+int kllm_gpu_prefill_v2(struct kllm_gpu_ctx *ctx,
+			const struct kllm_gpu_prefill_params *p);
+
 /* LSE merge of split-KV triples: for each of num_rows rows (seq x query
  * head), M = max_i m_i, w_i = l_i exp(m_i - M), out = sum_i w_i o_i / sum_i w_i
  * (0 when every l_i is 0). Inputs are stacked by part: m/l [num_parts]

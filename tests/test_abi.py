@@ -52,6 +52,7 @@ STRUCTS = {
     "kllm_gpu_attention_params_v2": kb.AttnParamsV2,
     "kllm_gpu_kv_append_params": kb.KvAppendParams,
     "kllm_gpu_gather_params": kb.GatherParams,
+    "kllm_gpu_prefill_params": kb.PrefillParams,
     "kllm_gpu_stats": kb.Stats,
 }
 

@@ -63,6 +63,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
 	return false;
 }
 
+__device__ __forceinline__ uint64_t global_ns()
+{
+	uint64_t t;
+	asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+	return t;
+}
+
+// Wait bounded by wall time (nanoseconds of the global timer) rather than
+// by a try count, for waits that complete in microseconds when healthy.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, uint64_t limit_ns)
+{
+	if (mbar_try_wait(bar, parity))
+		return true;
+	const uint64_t t0 = global_ns();
+	while (!mbar_try_wait(bar, parity))
+		if (global_ns() - t0 > limit_ns)
+			return false;
+	return true;
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src,

@@ -86,6 +86,29 @@ struct kllm_gather_args {
 };
 int kllm_gather_launch(const struct kllm_gather_args *a, void *stream);
 
+struct kllm_prefill_args {
+	void *out;                /* bf16 [num_tokens][num_heads][128] */
+	const void *q;            /* bf16 [num_tokens][num_heads][128] */
+	const void *k, *v;        /* bf16 [num_tokens][num_kv_heads][128] */
+	const int *cu_seqlens;    /* [num_seqs+1] */
+	const int *ctx_lens;      /* [num_seqs] */
+	const void *table;
+	int max_blocks;
+	int num_seqs, num_tokens, max_chunk;
+	int num_heads, num_kv_heads, head_dim;
+	int block_size, kv_dtype;
+	uint64_t layer_off;
+	float scale_log2;
+	uint32_t *err;
+};
+int kllm_prefill_launch(const struct kllm_prefill_args *a, void *stream);
+
+/* Quantize-on-write of a chunk: token i of sequence s (cu_seqlens[s] <= i <
+ * cu_seqlens[s+1]) goes to position ctx_lens[s] + i - cu_seqlens[s]. */
+int kllm_append_chunk_launch(const struct kllm_append_args *a,
+			     const int *cu_seqlens, const int *ctx_lens,
+			     void *stream);
+
 int kllm_merge_launch(const float *m, const float *l, const float *o,
 		      int num_parts, int num_rows, int head_dim, void *out,
 		      void *stream);

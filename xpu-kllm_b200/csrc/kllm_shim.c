@@ -664,6 +664,77 @@ int kllm_gpu_kv_append_v2(struct kllm_gpu_ctx *ctx,
 	return KLLM_OK;
 }
 
+int kllm_gpu_prefill_v2(struct kllm_gpu_ctx *ctx,
+			const struct kllm_gpu_prefill_params *p)
+{
+	if (!p || p->struct_size < sizeof(*p))
+		return fail(ctx, KLLM_EINVAL);
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (p->num_seqs < 0 || p->num_tokens < 0 || p->max_chunk < 0 || p->num_heads <= 0 ||
+	    p->num_kv_heads <= 0 || p->num_heads % p->num_kv_heads || p->max_blocks_per_seq <= 0)
+		return fail(ctx, KLLM_EINVAL);
+	int g = p->num_heads / p->num_kv_heads;
+	if (p->head_dim != 128 || (g != 1 && g != 2 && g != 4 && g != 8))
+		return fail(ctx, KLLM_ENOSYS);
+	if (p->block_size < 1 || p->block_size > 1024 ||
+	    (p->kv_dtype != KLLM_KV_BF16 && p->kv_dtype != KLLM_KV_MX_FP8_E4M3))
+		return fail(ctx, KLLM_ENOSYS);
+	if (p->num_seqs == 0 || p->num_tokens == 0)
+		return KLLM_OK;
+	if (!p->output || !p->q || !p->k || !p->v || !p->cu_seqlens || !p->ctx_lens ||
+	    !p->block_tables)
+		return fail(ctx, KLLM_EINVAL);
+	if ((((uintptr_t)p->q | (uintptr_t)p->k | (uintptr_t)p->v | (uintptr_t)p->output) & 15u) ||
+	    (p->layer_stride & 15u) || p->layer < 0)
+		return fail(ctx, KLLM_EINVAL);
+	cudaStream_t st = pick_stream(ctx, p->stream);
+	struct kllm_prefill_args a;
+	memset(&a, 0, sizeof(a));
+	a.out = p->output;
+	a.q = p->q;
+	a.k = p->k;
+	a.v = p->v;
+	a.cu_seqlens = p->cu_seqlens;
+	a.ctx_lens = p->ctx_lens;
+	a.table = p->block_tables;
+	a.max_blocks = p->max_blocks_per_seq;
+	a.num_seqs = p->num_seqs;
+	a.num_tokens = p->num_tokens;
+	a.max_chunk = p->max_chunk;
+	a.num_heads = p->num_heads;
+	a.num_kv_heads = p->num_kv_heads;
+	a.head_dim = p->head_dim;
+	a.block_size = p->block_size;
+	a.kv_dtype = p->kv_dtype;
+	a.layer_off = (uint64_t)p->layer * p->layer_stride;
+	a.scale_log2 = p->scale * 1.4426950408889634f;
+	a.err = p->err_word;
+	if (kllm_prefill_launch(&a, st))
+		return cuda_fail(ctx, cudaErrorLaunchFailure);
+	ctx->stats.launches++;
+	if (p->append) {
+		struct kllm_append_args b;
+		memset(&b, 0, sizeof(b));
+		b.k = p->k;
+		b.v = p->v;
+		b.num_tokens = p->num_tokens;
+		b.num_seqs = p->num_seqs;
+		b.table = p->block_tables;
+		b.max_blocks = p->max_blocks_per_seq;
+		b.num_kv_heads = p->num_kv_heads;
+		b.head_dim = p->head_dim;
+		b.block_size = p->block_size;
+		b.kv_dtype = p->kv_dtype;
+		b.layer_off = a.layer_off;
+		b.err = p->err_word;
+		if (kllm_append_chunk_launch(&b, p->cu_seqlens, p->ctx_lens, st))
+			return cuda_fail(ctx, cudaErrorLaunchFailure);
+		ctx->stats.launches++;
+	}
+	return KLLM_OK;
+}
+
 int kllm_gpu_gather_debug(struct kllm_gpu_ctx *ctx,
 			  const struct kllm_gpu_gather_params *p)
 {

@@ -69,21 +69,11 @@ __device__ __forceinline__ uint32_t mx_scale_code(float amax)
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// One thread = one 8-element micro-block of one (token, K|V, kv head) row.
-__global__ void append_kernel(const kllm_append_args a)
+// One 8-element micro-block b of kv head h of row i (K if kv == 0, else V),
+// written to position pos of sequence seq.
+__device__ __forceinline__ void append_block(const kllm_append_args &a, int i, int seq,
+					     int pos, int h, int kv, int b)
 {
-	const int nb = a.head_dim / 8;
-	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
-	if (t >= total)
-		return;
-	const int b = (int)(t % nb);
-	const long long r = t / nb;
-	const int h = (int)(r % a.num_kv_heads);
-	const int kv = (int)((r / a.num_kv_heads) % 2);
-	const int i = (int)(r / (2LL * a.num_kv_heads));
-
-	const int seq = a.token_seq[i], pos = a.token_pos[i];
 	const int blk = pos >= 0 ? pos / a.block_size : -1;
 	if (seq < 0 || seq >= a.num_seqs || blk < 0 || blk >= a.max_blocks) {
 		if (a.err && b == 0)
@@ -153,6 +143,51 @@ __global__ void append_kernel(const kllm_append_args a)
 	*reinterpret_cast<uint4 *>(sec + ((size_t)slot * d + b * 8) * 2) =
 	    make_uint4(outw[0], outw[1], outw[2], outw[3]);
 	sec[(size_t)bs * d * 2 + (size_t)slot * (d / 8) + b] = amax > 0.f ? 64 : 0;
+}
+
+// One thread = one 8-element micro-block of one (token, K|V, kv head) row.
+__global__ void append_kernel(const kllm_append_args a)
+{
+	const int nb = a.head_dim / 8;
+	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
+	if (t >= total)
+		return;
+	const int b = (int)(t % nb);
+	const long long r = t / nb;
+	const int h = (int)(r % a.num_kv_heads);
+	const int kv = (int)((r / a.num_kv_heads) % 2);
+	const int i = (int)(r / (2LL * a.num_kv_heads));
+	append_block(a, i, a.token_seq[i], a.token_pos[i], h, kv, b);
+}
+
+// Same, with the (sequence, position) of row i derived from chunk offsets.
+__global__ void append_chunk_kernel(const kllm_append_args a, const int *cu, const int *ctx)
+{
+	const int nb = a.head_dim / 8;
+	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
+	if (t >= total)
+		return;
+	const int b = (int)(t % nb);
+	const long long r = t / nb;
+	const int h = (int)(r % a.num_kv_heads);
+	const int kv = (int)((r / a.num_kv_heads) % 2);
+	const int i = (int)(r / (2LL * a.num_kv_heads));
+	int lo = 0, hi = a.num_seqs - 1;   // last s with cu[s] <= i
+	while (lo < hi) {
+		const int mid = (lo + hi + 1) >> 1;
+		if (cu[mid] <= i)
+			lo = mid;
+		else
+			hi = mid - 1;
+	}
+	if (i >= cu[lo + 1]) {             // i beyond the last chunk
+		if (a.err && b == 0)
+			atomicOr(a.err, 0x4u);
+		return;
+	}
+	append_block(a, i, lo, ctx[lo] + (i - cu[lo]), h, kv, b);
 }
 
 // One warp per (seq, kv head): walk the pages in order, skip invalid
@@ -264,6 +299,20 @@ extern "C" int kllm_append_launch(const struct kllm_append_args *a, void *stream
 	const int threads = 256;
 	const long long blocks = (total + threads - 1) / threads;
 	append_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+	return (int)cudaGetLastError();
+}
+
+extern "C" int kllm_append_chunk_launch(const struct kllm_append_args *a,
+					const int *cu_seqlens, const int *ctx_lens,
+					void *stream)
+{
+	const long long total = (long long)a->num_tokens * 2 * a->num_kv_heads * (a->head_dim / 8);
+	if (total <= 0)
+		return 0;
+	const int threads = 256;
+	const long long blocks = (total + threads - 1) / threads;
+	append_chunk_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+	    *a, cu_seqlens, ctx_lens);
 	return (int)cudaGetLastError();
 }
 

@@ -65,6 +65,17 @@ class GatherParams(Structure):
                 ("stream", c_void_p)]
 
 
+class PrefillParams(Structure):
+    _fields_ = [("struct_size", c_uint32), ("flags", c_uint32), ("output", c_void_p),
+                ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("cu_seqlens", c_void_p),
+                ("ctx_lens", c_void_p), ("num_seqs", c_int), ("num_tokens", c_int),
+                ("max_chunk", c_int), ("num_heads", c_int), ("num_kv_heads", c_int),
+                ("head_dim", c_int), ("block_tables", c_void_p), ("max_blocks_per_seq", c_int),
+                ("block_size", c_int), ("kv_dtype", c_int), ("layer", c_int),
+                ("layer_stride", c_uint64), ("scale", c_float), ("append", c_int),
+                ("err_word", c_void_p), ("stream", c_void_p)]
+
+
 class Stats(Structure):
     _fields_ = [("launches", c_uint64), ("kv_bytes", c_uint64), ("errors", c_uint64),
                 ("last_error", c_int), ("device", c_int), ("num_sms", c_int)]
@@ -88,6 +99,7 @@ _SIGNATURES = [
     ("kllm_gpu_decode_workspace_size", c_uint64, [c_void_p, c_int, c_int]),
     ("kllm_gpu_kv_append_v2", c_int, [c_void_p, POINTER(KvAppendParams)]),
     ("kllm_gpu_gather_debug", c_int, [c_void_p, POINTER(GatherParams)]),
+    ("kllm_gpu_prefill_v2", c_int, [c_void_p, POINTER(PrefillParams)]),
     ("kllm_gpu_merge_partials", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("kllm_gpu_memcpy_d2h", c_int, [c_void_p, c_void_p, c_void_p, c_uint64]),
@@ -186,6 +198,13 @@ class Backend:
         for k, v in kw.items():
             setattr(p, k, v)
         return self.lib.kllm_gpu_kv_append_v2(self.ctx, ctypes.byref(p))
+
+    def prefill(self, **kw) -> int:
+        p = PrefillParams()
+        p.struct_size = ctypes.sizeof(PrefillParams)
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return self.lib.kllm_gpu_prefill_v2(self.ctx, ctypes.byref(p))
 
     def gather(self, **kw) -> int:
         p = GatherParams()
