@@ -448,6 +448,295 @@ def cpu_baseline_from_rig(rig, args) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# chunked prefill + KV append (C5)
+# ---------------------------------------------------------------------------
+
+PREFILL_METRIC = "chunked prefill + MX-FP8 KV append: prompt tokens/s (attention TFLOP/s)"
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+class PrefillRig:
+    """One layer of the C5 step resident on the GPU: the chunk's Q/K/V, the
+    cache (with the shared prefix chain already written), table and outputs."""
+
+    def __init__(self, cfg: wl.DecodeConfig, be, torch, device: int, seed: int = 0):
+        self.cfg, self.be, self.torch = cfg, be, torch
+        c = cfg
+        dev = torch.device("cuda", device)
+        self.ctx, self.chunk = wl.prefill_split(c)
+        self.n_tok = int(self.chunk.sum())
+        self.plan = wl.plan_prefill_pages(c, self.ctx, self.chunk, seed)
+        self.arena = torch.zeros(self.plan.n_slots * c.slot_bytes(), dtype=torch.uint8,
+                                 device=dev)
+        table = wl.block_table(self.plan, c, self.arena.data_ptr())
+        self.table = torch.from_numpy(table.view(np.uint8).copy()).to(dev)
+        cu = np.concatenate([[0], np.cumsum(self.chunk)]).astype(np.int32)
+        self.cu = torch.from_numpy(cu).to(dev)
+        self.ctx_d = torch.from_numpy(self.ctx.copy()).to(dev)
+        tok_seq = np.repeat(np.arange(c.batch, dtype=np.int32), self.chunk)
+        tok_pos = np.concatenate([np.arange(a, a + n, dtype=np.int32)
+                                  for a, n in zip(self.ctx, self.chunk)])
+        self.tok_seq = torch.from_numpy(tok_seq).to(dev)
+        self.tok_pos = torch.from_numpy(tok_pos).to(dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000003 + 29)
+        n = self.n_tok
+        self.q = torch.randn((n, c.hq, c.d), generator=g, device=dev).to(torch.bfloat16)
+        self.k = torch.randn((n, c.hkv, c.d), generator=g, device=dev).to(torch.bfloat16)
+        self.v = torch.randn((n, c.hkv, c.d), generator=g, device=dev).to(torch.bfloat16)
+        self.out = torch.zeros((n, c.hq, c.d), dtype=torch.bfloat16, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # the shared prefix chain: written once through the first hit's table row
+        hits = [s for s in range(c.batch) if self.ctx[s] > 0]
+        if hits:
+            L = int(self.ctx[hits[0]])
+            pk = torch.randn((L, c.hkv, c.d), generator=g, device=dev).to(torch.bfloat16)
+            pv = torch.randn((L, c.hkv, c.d), generator=g, device=dev).to(torch.bfloat16)
+            ts = torch.full((L,), hits[0], dtype=torch.int32, device=dev)
+            tp = torch.arange(L, dtype=torch.int32, device=dev)
+            rc = self.append_raw(pk, pv, ts, tp, L)
+            assert rc == 0, f"prefix append failed: {rc}"
+        torch.cuda.synchronize()
+
+    def append_raw(self, k, v, ts, tp, n, stream=None) -> int:
+        c = self.cfg
+        return self.be.append(k=k.data_ptr(), v=v.data_ptr(), token_seq=ts.data_ptr(),
+                              token_pos=tp.data_ptr(), num_tokens=n, num_seqs=c.batch,
+                              block_tables=self.table.data_ptr(),
+                              max_blocks_per_seq=self.plan.max_blocks, num_kv_heads=c.hkv,
+                              head_dim=c.d, block_size=c.block, kv_dtype=c.kv_dtype, layer=0,
+                              layer_stride=c.layer_stride(),
+                              stream=stream or self.torch.cuda.current_stream().cuda_stream)
+
+    def prefill(self, stream: int, append: int, q=None, k=None, v=None, out=None) -> None:
+        c = self.cfg
+        rc = self.be.prefill(
+            output=out or self.out.data_ptr(), q=q or self.q.data_ptr(),
+            k=k or self.k.data_ptr(), v=v or self.v.data_ptr(), cu_seqlens=self.cu.data_ptr(),
+            ctx_lens=self.ctx_d.data_ptr(), num_seqs=c.batch, num_tokens=self.n_tok,
+            max_chunk=int(self.chunk.max()), num_heads=c.hq, num_kv_heads=c.hkv, head_dim=c.d,
+            block_tables=self.table.data_ptr(), max_blocks_per_seq=self.plan.max_blocks,
+            block_size=c.block, kv_dtype=c.kv_dtype, layer=0, layer_stride=c.layer_stride(),
+            scale=c.scale, append=append, err_word=self.err.data_ptr(), stream=stream)
+        if rc != 0:
+            raise RuntimeError(f"prefill launch failed: {rc}")
+
+    def append(self, stream: int) -> None:
+        rc = self.append_raw(self.k, self.v, self.tok_seq, self.tok_pos, self.n_tok, stream)
+        if rc != 0:
+            raise RuntimeError(f"append launch failed: {rc}")
+
+    def flops(self) -> int:
+        return wl.prefill_flops(self.ctx, self.chunk, self.cfg.hq, self.cfg.d)
+
+    def append_bytes(self) -> int:
+        """BF16 K/V read + MX pages written (payload + scales), each once."""
+        c = self.cfg
+        return self.n_tok * c.hkv * 2 * (c.d * 2 + c.d + c.d // 8)
+
+
+def prefill_cpu_sample(qq, kk, vv, cfg, step_flops: int, n_tok: int, seconds: float,
+                       use_ref: bool) -> dict:
+    """The reference CPU attention (kllm_ace_attention, one call per causal
+    row, as the reference has no mask) on sampled rows of one prompt and one
+    kv head -- qq [n, G, d], kk/vv [n, d] bf16 bits -- scaled to the whole
+    step by FLOPs."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    g, n = cfg.group, len(kk)
+    rows = list(range(7, n, 16))
+    t0 = time.perf_counter()
+    flops = reps = 0
+    while True:
+        for j in rows:
+            oracle.attention(qq[j][:, None, :], kk[:j + 1, None], vv[:j + 1, None], 1, cfg.d,
+                             j + 1, g, cfg.scale, use_ref=use_ref)
+            flops += 4 * cfg.d * g * (j + 1)
+        reps += 1
+        if time.perf_counter() - t0 > seconds or reps >= 50:
+            break
+    rate = flops / (time.perf_counter() - t0)
+    return {"value": round(n_tok / (step_flops / rate), 2), "unit": "tokens/s", "cores": 1,
+            "kind": "reference" if use_ref else "port", "tflops": round(rate / 1e12, 6),
+            "sample": f"{len(rows)} causal rows of one {n}-token prompt x {g} heads of one "
+                      f"kv head, x {reps} reps; scaled to the step by FLOPs"}
+
+
+def _use_ref() -> bool:
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    return oracle.ref() is not None
+
+
+def run_prefill(args) -> None:
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ["KLLM_GPU_DEVICE"] = str(local)
+    import kllm_b200 as kb
+    be = kb.Backend()
+    if be.backend != kb.KLLM_GPU_CUDA:
+        raise RuntimeError("libkllm_gpu: no sm_100 device")
+    torch.cuda.set_stream(be.torch_stream())
+    cfg = wl.PREFILL_CONFIGS[args.config]
+    rig = PrefillRig(cfg, be, torch, local, args.seed)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    for _ in range(args.warmup):
+        rig.prefill(sp, append=0)
+        rig.append(sp)
+    torch.cuda.synchronize()
+
+    # device-timed region: the chunk's Q/K/V/O (940 MB) exceed the 126 MB L2
+    clk = Clocks(local)
+    clk.start()
+    launches0 = be.stats().launches
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(3 * args.steps)]
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        evs[3 * i].record(stream)
+        rig.prefill(sp, append=0)
+        evs[3 * i + 1].record(stream)
+        rig.append(sp)
+        evs[3 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = be.stats().launches - launches0
+    t_pf = [evs[3 * i].elapsed_time(evs[3 * i + 1]) for i in range(args.steps)]
+    t_ap = [evs[3 * i + 1].elapsed_time(evs[3 * i + 2]) for i in range(args.steps)]
+    t_ms = evs[0].elapsed_time(evs[-1])
+    assert int(rig.err.item()) == 0, f"prefill error word {int(rig.err.item()):#x}"
+
+    # end to end through the C ABI: pinned host Q/K/V in, O out, one
+    # prefill_v2 call with append per step
+    hq_, hk_, hv_ = (x.cpu().pin_memory() for x in (rig.q, rig.k, rig.v))
+    ho = torch.empty_like(rig.out, device="cpu").pin_memory()
+    lib, ctx = be.lib, be.ctx
+    dq = torch.empty_like(rig.q)
+    dk = torch.empty_like(rig.k)
+    dv = torch.empty_like(rig.v)
+    nb = {id(hq_): rig.q.numel() * 2, id(hk_): rig.k.numel() * 2, id(hv_): rig.v.numel() * 2}
+
+    def e2e_step():
+        for h, d in ((hq_, dq), (hk_, dk), (hv_, dv)):
+            lib.kllm_gpu_memcpy_h2d_async(ctx, d.data_ptr(), h.data_ptr(), nb[id(h)], sp)
+        rig.prefill(sp, append=1, q=dq.data_ptr(), k=dk.data_ptr(), v=dv.data_ptr())
+        lib.kllm_gpu_memcpy_d2h_async(ctx, ho.data_ptr(), rig.out.data_ptr(),
+                                      rig.out.numel() * 2, sp)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te_ms = e0.elapsed_time(e1)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        s_last = cfg.batch - 1                    # a full-length prompt
+        a0, n0 = int(rig.cu[s_last].item()), int(rig.chunk[s_last])
+
+        def host(x):
+            return x[a0:a0 + n0].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        cpu = prefill_cpu_sample(host(rig.q[:, 0:cfg.group]), host(rig.k[:, 0]),
+                                 host(rig.v[:, 0]), cfg, rig.flops(), rig.n_tok,
+                                 args.cpu_seconds, _use_ref())
+    if rank == 0:
+        tpeak, tkind = bf16_peak()
+        hpeak, hkind = peaks()
+        flops = rig.flops()
+        pf_ms = float(np.mean(t_pf))
+        ap_ms = float(np.mean(t_ap))
+        achieved = flops / (pf_ms * 1e-3) / 1e12
+        line = {
+            "metric": PREFILL_METRIC,
+            "value": round(rig.n_tok * args.steps / (t_ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded torch.randn BF16 Q/K/V ~ N(0,1))",
+            "config": {"workload": cfg.name, "prompts": cfg.batch, "prompt_len": cfg.ctx_lo,
+                       "shared_prefix_hits": int((rig.ctx > 0).sum()),
+                       "shared_prefix_tokens": int(rig.ctx.max()), "new_tokens": rig.n_tok,
+                       "hq": cfg.hq, "hkv": cfg.hkv, "head_dim": cfg.d, "block": cfg.block,
+                       "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)",
+                       "l2": "inputs larger than L2 (chunk Q/K/V/O 940 MB per step)"},
+            "attention_tflops": round(achieved, 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tpeak,
+                         "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4),
+                         "peak_kind": tkind, "traffic": None,
+                         "kernel": "prefill_kernel<4> (tcgen05, causal algorithmic FLOPs)",
+                         "launch_ms": round(pf_ms, 4)},
+            "append_roofline": {"bound": "hbm",
+                                "achieved": round(rig.append_bytes() / (ap_ms * 1e-3) / 1e9, 1),
+                                "peak": hpeak, "unit": "GB/s", "peak_kind": hkind,
+                                "frac": round(rig.append_bytes() / (ap_ms * 1e-3) / 1e9 / hpeak,
+                                              4),
+                                "kernel": "append_kernel", "launch_ms": round(ap_ms, 4)},
+            "e2e": {"value": round(rig.n_tok * args.steps / (te_ms * 1e-3), 1),
+                    "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(sum(nb.values())),
+                    "d2h_bytes_per_step": int(rig.out.numel() * 2)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
+    be.close()
+
+
+def run_reference_prefill(args) -> None:
+    """The reference CPU attention on the C5 sample (host arrays only)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cfg = wl.PREFILL_CONFIGS[args.config]
+    ctx, chunk = wl.prefill_split(cfg)
+    n_tok = int(chunk.sum())
+    n = int(chunk[-1])                            # a full-length prompt
+    q = wl.normal_bf16(args.seed, wl.ST_PQ, 0, (n, cfg.hq, cfg.d))[:, :cfg.group]
+    k = wl.normal_bf16(args.seed, wl.ST_PK, 0, (n, cfg.hkv, cfg.d))[:, 0]
+    v = wl.normal_bf16(args.seed, wl.ST_PV, 0, (n, cfg.hkv, cfg.d))[:, 0]
+    flops = wl.prefill_flops(ctx, chunk, cfg.hq, cfg.d)
+    use_ref = _use_ref()
+    per = args.cpu_seconds / max(1, args.steps)
+    for _ in range(min(args.warmup, 1)):
+        prefill_cpu_sample(q, k, v, cfg, flops, n_tok, 0.0, use_ref)
+    samples = [prefill_cpu_sample(q, k, v, cfg, flops, n_tok, per, use_ref)
+               for _ in range(args.steps)]
+    value = float(np.mean([x["value"] for x in samples]))
+    line = {
+        "impl": "reference", "metric": PREFILL_METRIC, "value": round(value, 2),
+        "unit": "tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * n_tok / value, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "prompts": cfg.batch, "prompt_len": cfg.ctx_lo},
+        "cpu_baseline": dict(samples[-1], value=round(value, 2)),
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 # reference arm (CPU)
 # ---------------------------------------------------------------------------
 
@@ -510,7 +799,8 @@ def main():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
-    ap.add_argument("--config", default=wl.C3.name, choices=list(wl.CONFIGS))
+    ap.add_argument("--config", default=wl.C3.name,
+                    choices=list(wl.CONFIGS) + list(wl.PREFILL_CONFIGS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -519,10 +809,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    prefill = args.config in wl.PREFILL_CONFIGS
     if args.impl == "reference":
-        run_reference(args)
+        (run_reference_prefill if prefill else run_reference)(args)
     else:
-        run_kllm(args)
+        (run_prefill if prefill else run_kllm)(args)
 
 
 if __name__ == "__main__":

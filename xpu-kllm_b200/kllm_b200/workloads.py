@@ -139,6 +139,49 @@ C4 = DecodeConfig("c4_mxfp8_b1_ctx131072_64q8kv", batch=1, hq=64, hkv=8, kv_dtyp
                   ctx_kind="fixed", ctx_lo=131072, ctx_hi=131072, mult_lo=0.5, mult_hi=4.0)
 CONFIGS = {c.name: c for c in (C1, C2, C3, C4)}
 
+# Chunked prefill + KV append: 16 prompts of 2048 tokens, BF16 Q/K/V ~ N(0,1),
+# written into an MX-FP8 cache; the first quarter of the prompts share a
+# 1024-token prefix chain already in the cache (content-addressed hits), so
+# they prefill only their last 1024 tokens over those shared pages.
+C5 = DecodeConfig("c5_prefill_b16_2048_mxfp8_prefix1024", batch=16, hq=32, hkv=8,
+                  kv_dtype=KV_MX_FP8, ctx_kind="fixed", ctx_lo=2048, ctx_hi=2048)
+C5_SHARED_PREFIX = 1024
+PREFILL_CONFIGS = {C5.name: C5}
+
+
+def prefill_split(cfg: DecodeConfig, shared_prefix: int = C5_SHARED_PREFIX):
+    """(cached context, chunk length) per prompt: the first batch/4 prompts
+    hit the shared prefix chain."""
+    n_hit = cfg.batch // 4
+    ctx = np.zeros(cfg.batch, np.int32)
+    ctx[:n_hit] = shared_prefix
+    chunk = np.full(cfg.batch, cfg.ctx_lo, np.int32) - ctx
+    return ctx, chunk
+
+
+def prefill_flops(ctx: np.ndarray, chunk: np.ndarray, hq: int, d: int) -> int:
+    """Causal attention FLOPs (QK^T and PV, 2 each per multiply-add): chunk
+    row j of a prompt attends to ctx + j + 1 keys."""
+    keys = 0
+    for c0, n in zip(ctx.tolist(), chunk.tolist()):
+        keys += n * c0 + n * (n + 1) // 2
+    return 4 * d * hq * keys
+
+
+def plan_prefill_pages(cfg: DecodeConfig, ctx: np.ndarray, chunk: np.ndarray, seed: int = 0,
+                       n_slots: int | None = None) -> PagePlan:
+    """Pages of every prompt; prompts with a cached context share one chain
+    of pages for it (the first prompt's), as content-addressed hits do."""
+    total = ctx + chunk
+    plan = plan_pages(cfg, total, seed, n_slots=n_slots)
+    hits = [s for s in range(len(ctx)) if ctx[s] > 0]
+    if hits:
+        npg = int(ctx[hits[0]]) // cfg.block
+        for s in hits[1:]:
+            assert int(ctx[s]) == int(ctx[hits[0]])
+            plan.slots[s, :npg] = plan.slots[hits[0], :npg]
+    return plan
+
 
 def context_lengths(cfg: DecodeConfig, seed: int = 0) -> np.ndarray:
     u = uniforms(stream_key(seed, ST_CTX), np.arange(cfg.batch, dtype=np.uint64))
