@@ -13,6 +13,7 @@
  */
 #define _GNU_SOURCE
 #include <dlfcn.h>
+#include <sched.h>
 #include <errno.h>
 #include <math.h>
 #include <stdlib.h>
@@ -834,10 +835,13 @@ int kllm_gpu_comm_get_unique_id(uint8_t id[128])
 }
 
 /* Polls the communicator until it leaves ncclInProgress or the deadline
- * passes; aborts it on expiry or error. */
+ * passes; aborts it on expiry or error. An enqueue finishes in microseconds,
+ * so the first 2 ms only yield the CPU between polls; after that the poll
+ * sleeps 100 us at a time. */
 static int comm_wait(struct kllm_gpu_ctx *ctx, int timeout_ms)
 {
-	double deadline = now_ms() + (timeout_ms > 0 ? timeout_ms : 60000);
+	double t0 = now_ms();
+	double deadline = t0 + (timeout_ms > 0 ? timeout_ms : 60000);
 	for (;;) {
 		ncclResult_t st = ncclInProgress;
 		if (ctx->nccl.get_async_error(ctx->comm, &st) != ncclSuccess)
@@ -849,7 +853,10 @@ static int comm_wait(struct kllm_gpu_ctx *ctx, int timeout_ms)
 			ctx->comm = NULL;
 			return st == ncclInProgress ? KLLM_ETIMEDOUT : KLLM_EIO;
 		}
-		nap_us(100);
+		if (now_ms() - t0 < 2.0)
+			sched_yield();
+		else
+			nap_us(100);
 	}
 }
 
@@ -938,7 +945,7 @@ int kllm_gpu_comm_merge(struct kllm_gpu_ctx *ctx, const float *m,
 				return fail(ctx, as == ncclSuccess || as == ncclInProgress ?
 						     KLLM_ETIMEDOUT : KLLM_EIO);
 			}
-			nap_us(20);
+			sched_yield();
 		}
 	}
 	return KLLM_OK;
