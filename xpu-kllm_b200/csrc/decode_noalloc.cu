@@ -138,7 +138,7 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	a.kv_dtype = p->kv_dtype;
 	a.layer_off = (uint64_t)p->layer * p->layer_stride;
 	a.scale_log2 = p->scale * 1.4426950408889634f *
-		       (p->kv_dtype == KLLM_KV_MX_FP8_E4M3 ? 256.0f : 1.0f);
+		       (p->kv_dtype == KLLM_KV_MX_FP8_E4M3 ? KLLM_MX_DEC_UNBIAS : 1.0f);
 	a.pm = p->partial_m;
 	a.pl = p->partial_l;
 	a.po = p->partial_o;

@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace kllm {
@@ -145,6 +146,62 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
 {
 	__nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
 	return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0,
+					uint32_t a1, uint32_t a2, uint32_t a3,
+					uint32_t b0, uint32_t b1)
+{
+	asm volatile(
+	    "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+	    "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+	    : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+	    : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi)
+{
+	__half2 v = __floats2half2_rn(lo, hi);
+	return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ uint32_t f16x2_mul(uint32_t a, uint32_t b)
+{
+	uint32_t d;
+	asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+	return d;
+}
+
+// Two E4M3 codes (bytes 0, 1 of the low or high half of w) -> f16x2, exact
+// (every E4M3 value is an f16 value); byte 0 lands in the low half.
+__device__ __forceinline__ uint32_t e4m3x2_lo_to_f16x2(uint32_t w)
+{
+	uint32_t d;
+	asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\t"
+	    "cvt.rn.f16x2.e4m3x2 %0, l;\n\t}" : "=r"(d) : "r"(w));
+	return d;
+}
+
+__device__ __forceinline__ uint32_t e4m3x2_hi_to_f16x2(uint32_t w)
+{
+	uint32_t d;
+	asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\t"
+	    "cvt.rn.f16x2.e4m3x2 %0, h;\n\t}" : "=r"(d) : "r"(w));
+	return d;
+}
+
+// f16x2 (both halves) of e4m3(code) / 4: the MX-FP8 decode scale. With the
+// 2^-2 factor, payload x scale <= 448 * 448 / 4 = 50176 stays an f16 value;
+// products of at least 2^-14 are exact, smaller ones are rounded to the f16
+// subnormal step 2^-24 (2^-22 after the factor is undone).
+__device__ __forceinline__ uint32_t mx_scale_lut_entry_f16(uint32_t code)
+{
+	const uint32_t e = (code >> 3) & 0xFu, m = code & 0x7u;
+	// (8 + m) * 2^(e - 10) for e > 0, m * 2^-9 for e == 0; then / 4
+	const float v = e ? (float)(8u + m) * __uint_as_float((e + 115u) << 23)
+			  : (float)m * __uint_as_float(116u << 23);
+	const uint32_t h = pack_f16x2(v, v);
+	return (code & 0x80u) ? (h | 0x80008000u) : h;
 }
 
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b)

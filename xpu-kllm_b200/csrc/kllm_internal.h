@@ -19,6 +19,9 @@ extern "C" {
 #define KLLM_MAX_SEQS_LAUNCH 4096 /* sequences per decode launch (smem prefix) */
 
 #define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
+/* MX-FP8 decode computes with K/V values scaled by 2^-2 (payload x scale
+ * stays below the f16 maximum); scores and outputs are multiplied back. */
+#define KLLM_MX_DEC_UNBIAS   4.0f
 
 struct kllm_decode_args {
 	void *out;                /* bf16 [S][Hq][D] or NULL */

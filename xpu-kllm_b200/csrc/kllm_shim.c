@@ -488,7 +488,7 @@ static void fill_args(struct kllm_decode_args *a, void *out, const void *q,
 	a->layer_off = layer_off;
 	/* log2 domain; MX tiles are dequantised with an extra 2^-8 */
 	a->scale_log2 = scale * 1.4426950408889634f *
-			(kv == KLLM_KV_MX_FP8_E4M3 ? 256.0f : 1.0f);
+			(kv == KLLM_KV_MX_FP8_E4M3 ? KLLM_MX_DEC_UNBIAS : 1.0f);
 }
 
 /* userspace/gpu/paged_attention.cu:121-146: v1 semantics, BF16 128-token pages. */

@@ -27,8 +27,11 @@
 //   S^T[16 tok x 8 heads] = K_tile[16 x D] . Q^T   (mma.m16n8k16, bf16)
 //   P^T -> bf16 hi + bf16 lo, transposed in registers (movmatrix)
 //   O^T[D x 8 heads] += V_tile^T[D x 16] . (P_hi^T + P_lo^T)  (2 x mma.m16n8k16)
-// MX-FP8 tiles are dequantised in registers to bf16 exactly (see
-// kllm_device.cuh). Dimensions are permuted consistently inside each
+// MX-FP8 tiles are dequantised in registers to f16 (hardware e4m3x2 -> f16x2
+// conversion, then one f16x2 multiply by the block's scale / 4) and the MX
+// contractions run as f16 MMAs; the query is scaled by a power of two into
+// f16 range per segment, and both factors are undone in the softmax scale
+// and the final normalisation. Dimensions are permuted consistently inside each
 // contraction so that every lane reads contiguous 16-byte runs of shared
 // memory; the output permutation is undone at the store.
 
@@ -241,13 +244,38 @@ __device__ __forceinline__ void load_q(uint32_t (&q)[D / 8],
 	}
 }
 
+// MX path: the segment's query rows (bf16, as load_q leaves them) -> f16,
+// multiplied by 2^e so that the largest |q| lies in [2^14, 2^15): no
+// overflow, and every bf16 value of at least 2^-28 of that maximum converts
+// exactly. Returns 2^-e, which multiplies the softmax scale.
+template <int D>
+__device__ __forceinline__ float q_to_f16(uint32_t (&q)[D / 8])
+{
+	float mx = 0.f;
+#pragma unroll
+	for (int i = 0; i < D / 8; ++i)
+		mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(q[i] << 16)),
+				     fabsf(__uint_as_float(q[i] & 0xFFFF0000u))));
+#pragma unroll
+	for (int off = 1; off < 32; off <<= 1)
+		mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+	const int E = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 0xFFu) - 127 : 0;
+	int e = 14 - E;
+	e = e < -100 ? -100 : (e > 100 ? 100 : e);
+	const float f = __uint_as_float((uint32_t)(e + 127) << 23);
+#pragma unroll
+	for (int i = 0; i < D / 8; ++i)
+		q[i] = pack_f16x2(__uint_as_float(q[i] << 16) * f,
+				  __uint_as_float(q[i] & 0xFFFF0000u) * f);
+	return __uint_as_float((uint32_t)(127 - e) << 23);
+}
+
 // One 16-token tile: scores, online-softmax update and PV accumulation.
 template <int D, int KVT>
 __device__ __forceinline__ void tile_compute(
     const uint8_t *sK, const uint8_t *sV, const uint32_t *lut, int ntok,
     const uint32_t (&q)[D / 8], float (&o)[D / 16][4], float &m0, float &m1,
-    float &l0, float &l1, float &mx0, float &mx1, float scale_log2, int lane,
-    uint32_t k16, uint32_t k2p28)
+    float &l0, float &l1, float &mx0, float &mx1, float scale_log2, int lane)
 {
 	using Gm = Geom<D, KVT>;
 	const int g = lane >> 2, c = lane & 3;
@@ -276,17 +304,15 @@ __device__ __forceinline__ void tile_compute(
 		}
 #pragma unroll
 		for (int j = 0; j < D / 16; ++j) {
-			uint32_t r0lo, r0hi, r1lo, r1hi;
-			e4m3x4_to_bf16x2_raw(k0[j], k16, k2p28, r0lo, r0hi);
-			e4m3x4_to_bf16x2_raw(k1[j], k16, k2p28, r1lo, r1hi);
-			const uint32_t a0 = bf16x2_mul(r0lo, sc0[j >> 1]);
-			const uint32_t a2 = bf16x2_mul(r0hi, sc0[j >> 1]);
-			const uint32_t a1 = bf16x2_mul(r1lo, sc1[j >> 1]);
-			const uint32_t a3 = bf16x2_mul(r1hi, sc1[j >> 1]);
+			// word j = dims 4j..4j+3 of this lane's chunk: (0,1) -> a0/a1, (2,3) -> a2/a3
+			const uint32_t a0 = f16x2_mul(e4m3x2_lo_to_f16x2(k0[j]), sc0[j >> 1]);
+			const uint32_t a2 = f16x2_mul(e4m3x2_hi_to_f16x2(k0[j]), sc0[j >> 1]);
+			const uint32_t a1 = f16x2_mul(e4m3x2_lo_to_f16x2(k1[j]), sc1[j >> 1]);
+			const uint32_t a3 = f16x2_mul(e4m3x2_hi_to_f16x2(k1[j]), sc1[j >> 1]);
 			if (j & 1)
-				mma_bf16(s2, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
+				mma_f16(s2, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
 			else
-				mma_bf16(s, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
+				mma_f16(s, a0, a1, a2, a3, q[2 * j], q[2 * j + 1]);
 		}
 	} else {
 		constexpr int KW = D / 8;
@@ -344,13 +370,25 @@ __device__ __forceinline__ void tile_compute(
 	const float p1 = exp2f(x1 - m1), p3 = exp2f(x3 - m1);
 	l0 += p0 + p2;
 	l1 += p1 + p3;
-	// P as bf16 hi + bf16 lo (16 significant bits): a bf16-only P misses the
-	// 1e-3 absolute bound on outputs built from large, cancelling V values.
-	const uint32_t h01 = pack_bf16x2(p0, p1), h23 = pack_bf16x2(p2, p3);
-	const uint32_t l01 = pack_bf16x2(p0 - __uint_as_float(h01 << 16),
-					 p1 - __uint_as_float(h01 & 0xFFFF0000u));
-	const uint32_t l23 = pack_bf16x2(p2 - __uint_as_float(h23 << 16),
-					 p3 - __uint_as_float(h23 & 0xFFFF0000u));
+	// P as a hi + lo pair of the V operand's type (bf16: 16 significant bits,
+	// f16: 22): one rounded P misses the 1e-3 absolute bound on outputs built
+	// from a few large, cancelling V values.
+	uint32_t h01, h23, l01, l23;
+	if constexpr (Gm::MX) {
+		h01 = pack_f16x2(p0, p1);
+		h23 = pack_f16x2(p2, p3);
+		const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
+		const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
+		l01 = pack_f16x2(p0 - f01.x, p1 - f01.y);
+		l23 = pack_f16x2(p2 - f23.x, p3 - f23.y);
+	} else {
+		h01 = pack_bf16x2(p0, p1);
+		h23 = pack_bf16x2(p2, p3);
+		l01 = pack_bf16x2(p0 - __uint_as_float(h01 << 16),
+				  p1 - __uint_as_float(h01 & 0xFFFF0000u));
+		l23 = pack_bf16x2(p2 - __uint_as_float(h23 << 16),
+				  p3 - __uint_as_float(h23 & 0xFFFF0000u));
+	}
 	const uint32_t b0 = movmatrix_trans(h01);   // tok 2c,2c+1;   head g
 	const uint32_t b1 = movmatrix_trans(h23);   // tok 2c+8,2c+9; head g
 	const uint32_t c0 = movmatrix_trans(l01);
@@ -392,23 +430,19 @@ __device__ __forceinline__ void tile_compute(
 			const uint32_t c01b = __byte_perm(w0[i], w1[i], 0x7362u);
 			const uint32_t c23a = __byte_perm(w2[i], w3[i], 0x5140u);
 			const uint32_t c23b = __byte_perm(w2[i], w3[i], 0x7362u);
-			uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
-			e4m3x4_to_bf16x2_raw(c01a, k16, k2p28, x0, x1);  // (R0,R1) bytes 0 | 1
-			e4m3x4_to_bf16x2_raw(c23a, k16, k2p28, x2, x3);
-			e4m3x4_to_bf16x2_raw(c01b, k16, k2p28, y0, y1);  // (R0,R1) bytes 2 | 3
-			e4m3x4_to_bf16x2_raw(c23b, k16, k2p28, y2, y3);
-			const uint32_t e0 = bf16x2_mul(x0, s01[bb]);
-			const uint32_t e1 = bf16x2_mul(x1, s01[bb]);
-			const uint32_t e2 = bf16x2_mul(x2, s23[bb]);
-			const uint32_t e3 = bf16x2_mul(x3, s23[bb]);
-			mma_bf16(o[2 * i], e0, e1, e2, e3, b0, b1);
-			mma_bf16(o[2 * i], e0, e1, e2, e3, c0, c1);
-			const uint32_t f0 = bf16x2_mul(y0, s01[bb]);
-			const uint32_t f1 = bf16x2_mul(y1, s01[bb]);
-			const uint32_t f2 = bf16x2_mul(y2, s23[bb]);
-			const uint32_t f3 = bf16x2_mul(y3, s23[bb]);
-			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, b0, b1);
-			mma_bf16(o[2 * i + 1], f0, f1, f2, f3, c0, c1);
+			// (R0,R1) / (R2,R3) token pairs of dims 4i, 4i+1 (x) and 4i+2, 4i+3 (y)
+			const uint32_t e0 = f16x2_mul(e4m3x2_lo_to_f16x2(c01a), s01[bb]);
+			const uint32_t e1 = f16x2_mul(e4m3x2_hi_to_f16x2(c01a), s01[bb]);
+			const uint32_t e2 = f16x2_mul(e4m3x2_lo_to_f16x2(c23a), s23[bb]);
+			const uint32_t e3 = f16x2_mul(e4m3x2_hi_to_f16x2(c23a), s23[bb]);
+			mma_f16(o[2 * i], e0, e1, e2, e3, b0, b1);
+			mma_f16(o[2 * i], e0, e1, e2, e3, c0, c1);
+			const uint32_t f0 = f16x2_mul(e4m3x2_lo_to_f16x2(c01b), s01[bb]);
+			const uint32_t f1 = f16x2_mul(e4m3x2_hi_to_f16x2(c01b), s01[bb]);
+			const uint32_t f2 = f16x2_mul(e4m3x2_lo_to_f16x2(c23b), s23[bb]);
+			const uint32_t f3 = f16x2_mul(e4m3x2_hi_to_f16x2(c23b), s23[bb]);
+			mma_f16(o[2 * i + 1], f0, f1, f2, f3, b0, b1);
+			mma_f16(o[2 * i + 1], f0, f1, f2, f3, c0, c1);
 		}
 	} else {
 		constexpr int VW = D / 16;
@@ -585,11 +619,7 @@ decode_kernel(const kllm_decode_args a)
 	// ---- per-CTA setup: scale LUT, clamped lengths, tile prefix sums -------
 	if constexpr (Gm::MX)
 		for (int i = tid; i < 256; i += blockDim.x)
-			lut[i] = mx_scale_lut_entry((uint32_t)i);
-	if (tid == 0) {
-		lut[256] = 16u;        // multiplier constants for the dequant, read
-		lut[257] = 1u << 28;   // back at run time (kept out of immediates)
-	}
+			lut[i] = mx_scale_lut_entry_f16((uint32_t)i);
 	{
 		bool too_long = false;
 		const int cap = a.max_blocks * a.block_size;
@@ -663,7 +693,7 @@ decode_kernel(const kllm_decode_args a)
 	const uint64_t policy = l2_evict_first_policy();
 	const size_t sec = Gm::MX ? (size_t)a.block_size * D * 9 / 8
 				  : (size_t)a.block_size * D * 2;
-	const float unbias = Gm::MX ? kMxUnbias : 1.f;
+	const float unbias = Gm::MX ? KLLM_MX_DEC_UNBIAS : 1.f;
 
 	// ---- producer: block-table batches and the bulk-copy ring --------------
 	Batch cur, nxt;
@@ -723,6 +753,9 @@ decode_kernel(const kllm_decode_args a)
 	int piece_j0 = cc.j;
 	uint32_t q[D / 8];
 	load_q<D>(q, a, cc.s, cc.h, lane);
+	float sl2 = a.scale_log2;
+	if constexpr (Gm::MX)
+		sl2 = a.scale_log2 * q_to_f16<D>(q);
 	float o[D / 16][4];
 #pragma unroll
 	for (int mt = 0; mt < D / 16; ++mt)
@@ -730,7 +763,6 @@ decode_kernel(const kllm_decode_args a)
 	float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
 	float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
 	const int g = lane >> 2, c = lane & 3;
-	const uint32_t k16 = lut[256], k2p28 = lut[257];
 
 	for (int i = 0; i < n; ++i) {
 		if (p < n) {
@@ -747,8 +779,7 @@ decode_kernel(const kllm_decode_args a)
 		if (ntok > 0) {
 			const uint8_t *sK = wst + (size_t)st * Gm::STAGE;
 			tile_compute<D, KVT>(sK, sK + Gm::KV, lut, ntok, q, o, m0,
-					     m1, l0, l1, mx0, mx1, a.scale_log2, lane, k16,
-					     k2p28);
+					     m1, l0, l1, mx0, mx1, sl2, lane);
 		}
 		__syncwarp();
 
@@ -875,6 +906,8 @@ decode_kernel(const kllm_decode_args a)
 		piece_j0 = 0;
 		piece_x0 = xa + i + 1;
 		load_q<D>(q, a, cc.s, cc.h, lane);
+		if constexpr (Gm::MX)
+			sl2 = a.scale_log2 * q_to_f16<D>(q);
 #pragma unroll
 		for (int mt = 0; mt < D / 16; ++mt)
 			o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
@@ -1042,7 +1075,7 @@ extern "C" int kllm_decode_merge_launch(const struct kllm_decode_args *a,
 	if (!a->ws_list || !a->split)
 		return 0;
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
-	const float unbias = a->kv_dtype ? kMxUnbias : 1.f;
+	const float unbias = a->kv_dtype ? KLLM_MX_DEC_UNBIAS : 1.f;
 	const int grid = num_sms > 0 ? num_sms : 148;
 	if (a->head_dim == 128)
 		merge_big_kernel<128><<<grid, 256, 0, st>>>(*a, unbias);
