@@ -39,6 +39,13 @@ from kllm_b200 import workloads as wl  # noqa: E402
 
 METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200"
 
+# DRAM bytes per decode launch / algorithmic bytes, from one ncu capture of
+# decode_kernel<128,1> on the C2 workload (64 requests, 350.9 MB algorithmic):
+# 351.9 MB read + 4.7 MB written (outputs and split-KV partials). Traffic
+# grows with the bytes processed, so a launch of B algorithmic bytes moves
+# about B x this ratio.
+DECODE_TRAFFIC_RATIO = 1.0162
+
 
 def peaks() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -63,7 +70,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -102,7 +109,8 @@ class DecodeRig:
     """The rank's requests resident on its GPU: pages, table, Q, outputs."""
 
     def __init__(self, cfg: wl.DecodeConfig, seqs: list[int], all_lens: np.ndarray, be,
-                 torch, device: int, seed: int = 0, arena_factor: float = 1.25):
+                 torch, device: int, seed: int = 0, arena_factor: float = 1.25,
+                 layer_major: bool = True):
         self.cfg, self.be, self.torch = cfg, be, torch
         self.seqs = seqs
         self.lens = np.asarray(all_lens)[seqs].astype(np.int32)
@@ -119,7 +127,13 @@ class DecodeRig:
         self.arena_bytes = n_slots * slot_b
         self.plan = wl.plan_pages(c, self.lens, seed, n_slots=n_slots)
         self.arena = torch.empty(self.arena_bytes, dtype=torch.uint8, device=dev)
-        table = wl.block_table(self.plan, c, self.arena.data_ptr())
+        # layer-major: layer l of every slot is one contiguous region, so a
+        # launch (one layer) touches n_slots x 36 KB instead of 36 KB in each
+        # 1.18 MB all-layer slot (far fewer GPU pages per launch)
+        self.layer_major = layer_major
+        self.slot_pitch = c.layer_stride() if layer_major else slot_b
+        self.layer_stride = n_slots * c.layer_stride() if layer_major else c.layer_stride()
+        table = wl.block_table(self.plan, c, self.arena.data_ptr(), slot_pitch=self.slot_pitch)
         self.table = torch.from_numpy(table.view(np.uint8).copy()).to(dev)
         self.seq_lens = torch.from_numpy(self.lens.copy()).to(dev)
         g = torch.Generator(device=dev)
@@ -155,7 +169,7 @@ class DecodeRig:
                                     max_blocks_per_seq=self.plan.max_blocks,
                                     num_kv_heads=c.hkv, head_dim=c.d, block_size=c.block,
                                     kv_dtype=c.kv_dtype, layer=layer,
-                                    layer_stride=c.layer_stride(), stream=st)
+                                    layer_stride=self.layer_stride, stream=st)
                 assert rc == 0, f"append failed: {rc}"
         torch.cuda.synchronize()
 
@@ -190,7 +204,7 @@ class DecodeRig:
             block_tables=self.table.data_ptr(), seq_lens=self.seq_lens.data_ptr(),
             num_seqs=self.B, num_heads=c.hq, num_kv_heads=c.hkv, head_dim=c.d,
             max_blocks_per_seq=self.plan.max_blocks, block_size=c.block, kv_dtype=c.kv_dtype,
-            layer=layer, layer_stride=c.layer_stride(), scale=c.scale, split=1, stream=stream)
+            layer=layer, layer_stride=self.layer_stride, scale=c.scale, split=1, stream=stream)
         if self.split_kv:
             kw.update(output=None, partial_m=self.pm.data_ptr(), partial_l=self.pl.data_ptr(),
                       partial_o=self.po.data_ptr())
@@ -217,12 +231,11 @@ class DecodeRig:
         plan_rows = self.plan.slots[seqs_local]
         used = plan_rows[plan_rows >= 0]
         host = np.zeros((len(used), c1.slot_bytes()), dtype=np.uint8)
-        slot_b = c.slot_bytes()
         arena_view = self.arena.view(-1)
-        loff = layer * c.layer_stride()
+        loff = layer * self.layer_stride
         remap = {}
         for i, sl in enumerate(used):
-            a = int(sl) * slot_b + loff
+            a = int(sl) * self.slot_pitch + loff
             host[i] = arena_view[a:a + c.layer_stride()].cpu().numpy()
             remap[int(sl)] = i
         slots = np.full(plan_rows.shape, -1, np.int64)
@@ -273,7 +286,8 @@ def run_kllm(args) -> None:
     else:
         mine = mg.lpt_shard(lens_all, world)[rank]
         lens_rank = lens_all
-    rig = DecodeRig(cfg, mine, lens_rank, be, torch, local, args.seed)
+    rig = DecodeRig(cfg, mine, lens_rank, be, torch, local, args.seed,
+                    layer_major=args.arena_layout == "layer-major")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     if split_kv:
@@ -294,24 +308,22 @@ def run_kllm(args) -> None:
     clk = Clocks(local)
     clk.start()
     launches0 = be.stats().launches
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * cfg.layers + 1)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     barrier()
     t0.record(stream)
-    k = 0
     for _ in range(args.steps):
         for layer in range(cfg.layers):
-            ev[k].record(stream)
             rig.launch(layer, sp)
-            k += 1
-    ev[k].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
     clocks = clk.stop()
     launches = be.stats().launches - launches0
     elapsed_ms = t0.elapsed_time(t1)
-    per_launch = [ev[i].elapsed_time(ev[i + 1]) for i in range(k)]
+    # mean decode launch = the timed region / decode launches: only the decode
+    # (and its merge, which is empty unless a segment has > 16 pieces) runs
+    # there; an event pair around every launch would cost 1-4% by itself
+    per_launch = [elapsed_ms / (args.steps * cfg.layers)]
 
     # end-to-end through the C ABI: pinned host Q in, bf16 O out, every step
     host_q = torch.empty_like(rig.q, device="cpu").pin_memory()
@@ -384,6 +396,7 @@ def run_kllm(args) -> None:
                        "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)",
                        "kv_gb_per_step": round(total_bytes / 1e9, 3),
                        "arena_gb_rank0": round(float(allst[0, 5]) / 1e9, 2),
+                       "arena_layout": args.arena_layout,
                        "l2": "inputs larger than L2 (KV per step >> 126 MB)",
                        "parallelism": (f"split-KV x{world} (page ranges) + NCCL all-gather "
                                        f"merge" if split_kv else
@@ -392,7 +405,10 @@ def run_kllm(args) -> None:
             "hbm_frac_8tbs": round(value / world / 8000.0, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind,
+                         "traffic": round(per_launch_bytes * DECODE_TRAFFIC_RATIO),
+                         "traffic_source": "ncu dram__bytes_read+write of the C2 workload, "
+                                           "scaled by algorithmic bytes per launch",
                          "kernel": "decode_kernel<128,1> (MX-FP8)"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(cfg.layers * qb + rig.B * 4),
@@ -804,6 +820,10 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--arena-layout", default="layer-major",
+                    choices=["layer-major", "slot-major"],
+                    help="layer-major: each layer's pages form one region (layer_stride = "
+                         "n_slots x 2 pages); slot-major: a slot holds all layers of a block")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (smaller captures for profiling)")
     args = ap.parse_args()

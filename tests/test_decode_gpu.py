@@ -216,6 +216,26 @@ def test_layers_and_golden_c1(be):
     kvcase.assert_close_bf16(run_v2(be, dc1), golden.load()["c1_out"], what="C1 golden")
 
 
+def test_layer_major_arena(be):
+    """The same pages laid out layer-major (layer l of every slot in one
+    region: slot pitch = one layer's K+V pages, layer stride = n_slots x
+    that), decoded for each layer through the ABI's layer stride."""
+    import torch
+    cfg = replace(wl.C2, batch=5, layers=3)
+    hc = kvcase.build_case(cfg, seq_lens=[700, 16, 1, 2049, 333])
+    c = hc.cfg
+    n = hc.plan.n_slots
+    pair = c.layer_stride()
+    lm = hc.arena.reshape(n, c.layers, pair).transpose(1, 0, 2).copy()
+    dc = kvcase.DeviceCase(hc)
+    arena = torch.from_numpy(lm).cuda()
+    table = wl.block_table(hc.plan, c, arena.data_ptr(), hc.valid, slot_pitch=pair)
+    dc.table = torch.from_numpy(table.view(np.uint8).copy()).cuda()
+    for layer in range(c.layers):
+        got = run_v2(be, dc, layer=layer, layer_stride=n * pair)
+        kvcase.assert_close_bf16(got, hc.oracle_decode(layer=layer), what=f"layer {layer}")
+
+
 def test_seq_too_long_flag_and_clamp(be):
     import torch
     cfg = replace(wl.C1, arena_slots=None)

@@ -236,11 +236,16 @@ def plan_pages(cfg: DecodeConfig, seq_lens: np.ndarray, seed: int = 0,
                     max_blocks=mb, pages_used=need)
 
 
-def block_table(plan: PagePlan, cfg: DecodeConfig, base: int, valid=None) -> np.ndarray:
-    """Entries {k_ptr, v_ptr, valid} for an arena at address ``base``."""
+def block_table(plan: PagePlan, cfg: DecodeConfig, base: int, valid=None,
+                slot_pitch: int | None = None) -> np.ndarray:
+    """Entries {k_ptr, v_ptr, valid} for an arena at address ``base``.
+    ``slot_pitch``: bytes between consecutive slots (default: a slot holds
+    every layer, ``cfg.slot_bytes()``; a layer-major arena passes
+    ``cfg.layer_stride()`` and a layer stride of n_slots x that)."""
     t = np.zeros(plan.slots.shape, dtype=ENTRY_DTYPE)
     used = plan.slots >= 0
-    addr = np.uint64(base) + plan.slots.clip(0).astype(np.uint64) * np.uint64(cfg.slot_bytes())
+    pitch = cfg.slot_bytes() if slot_pitch is None else slot_pitch
+    addr = np.uint64(base) + plan.slots.clip(0).astype(np.uint64) * np.uint64(pitch)
     t["k"] = np.where(used, addr, 0)
     t["v"] = np.where(used, addr + np.uint64(cfg.page_bytes()), 0)
     t["valid"] = used.astype(np.int32) if valid is None else (used & valid).astype(np.int32)
