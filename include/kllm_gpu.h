@@ -355,6 +355,7 @@ struct kllm_gpu_stats {
 	int last_error;              /* last negative return code */
 	int device;                  /* CUDA ordinal */
 	int num_sms;
+	int last_cuda_error;         /* cudaError_t behind the last KLLM_EIO (0: none) */
 };
 int kllm_gpu_get_stats(struct kllm_gpu_ctx *ctx, struct kllm_gpu_stats *out);
 

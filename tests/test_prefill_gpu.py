@@ -102,7 +102,7 @@ def _run(be, hc, ctx_lens, chunk_lens, cu, q, k, v, append=1):
                     kv_dtype=c.kv_dtype, layer=0, layer_stride=c.layer_stride(), scale=c.scale,
                     append=append, err_word=err.data_ptr(),
                     stream=torch.cuda.current_stream().cuda_stream)
-    assert rc == 0, rc
+    assert rc == 0, (rc, "cuda error", be.stats().last_cuda_error)
     torch.cuda.synchronize()
     assert int(err.item()) == 0, hex(int(err.item()))
     return out.cpu().numpy().view(np.uint16), dc.arena.cpu().numpy()

@@ -77,8 +77,9 @@ static int fail(struct kllm_gpu_ctx *ctx, int code)
 
 static int cuda_fail(struct kllm_gpu_ctx *ctx, cudaError_t e)
 {
-	(void)cudaGetLastError();  /* clear a non-sticky error */
-	(void)e;
+	cudaError_t last = cudaGetLastError();  /* clears a non-sticky error */
+	if (ctx)
+		ctx->stats.last_cuda_error = (int)(e != cudaSuccess ? e : last);
 	return fail(ctx, KLLM_EIO);
 }
 
@@ -711,8 +712,9 @@ int kllm_gpu_prefill_v2(struct kllm_gpu_ctx *ctx,
 	a.layer_off = (uint64_t)p->layer * p->layer_stride;
 	a.scale_log2 = p->scale * 1.4426950408889634f;
 	a.err = p->err_word;
-	if (kllm_prefill_launch(&a, st))
-		return cuda_fail(ctx, cudaErrorLaunchFailure);
+	int le = kllm_prefill_launch(&a, st);
+	if (le)
+		return cuda_fail(ctx, (cudaError_t)le);
 	ctx->stats.launches++;
 	if (p->append) {
 		struct kllm_append_args b;

@@ -9,23 +9,29 @@
 // semantics are those of its CPU attention (userspace/compute/ace_attention.c:
 // 85-134) applied row by row with keys [0, position].
 //
-// One CTA (4 warps) per (sequence, kv head, block of 128/G chunk positions).
-// Its 128 matrix rows are (query head of the group, position): row r = h *
-// (128/G) + p, so the K/V tiles are shared by the G heads of the group.
-// Per 128-key block:
-//   S[128 x 128] = Q . K^T          tcgen05.mma kind::f16, D in TMEM
-//   P = exp2(S*scale - m)           each thread owns one row (TMEM lane)
-//   O[128 x 128] += P . V           tcgen05.mma, A = P (smem), B = V (MN-major)
-// P enters the product as two bf16 terms (P_hi + P_lo, residual ~2^-17 |P|),
-// issued as one K = 256 accumulation over the same V tile.
-// Q, K, V and P live in shared memory in the 128-byte-swizzled K-major
-// (V: MN-major) canonical layouts. Chunk K/V tiles arrive by TMA tensor
-// copies; cached-context tiles are dequantised into the same layout by the
-// threads (MX: exact bf16 values, see kllm_device.cuh).
+// One CTA per (sequence, kv head, 2 x 128/G chunk positions) holds two query
+// tiles A and B of 128 MMA rows each (row r = h * (128/G) + p: head h of the
+// group, position p), which share every K/V block. Per 128-key block j:
+//   S_t = Q_t . K_j^T        tcgen05.mma kind::f16, Q and K in shared memory
+//   P_t = exp2(S_t*c - m)    one softmax thread per row (TMEM lane), written
+//                            back over S_t as bf16 hi + lo
+//   O_t += P_t . V_j         tcgen05.mma with A = P_t read from TMEM
+// Warp roles (13 warps):
+//   0-3 / 4-7  softmax of tile A / B (warp w reads TMEM lanes 32 (w % 4) ..)
+//   8-11       producer: Q tiles, then per block either TMA tensor copies of
+//              the chunk's K/V or the exact dequant of cached pages
+//   12         TMEM allocation and MMA issue (one lane)
+// K/V blocks go through a 2-stage ring, so the tensor core runs one tile's
+// PV and next S while the other tile's softmax runs. TMEM: S_A, S_B, O_A,
+// O_B, 128 fp32 columns each. Every wait is bounded in wall time and can be
+// aborted; a timeout sets KLLM_ERR_TIMEOUT, drains the CTA's own copies and
+// MMAs, frees TMEM and leaves the CTA.
 
 #include "kllm_device.cuh"
 #include "kllm_internal.h"
 
+#include <cstdio>
+#include <cstdlib>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math_constants.h>
@@ -42,17 +48,23 @@ constexpr int kHalfBytes = kTileBytes / 2;    // 16 KB: one 64-column half
 constexpr float kLazyLog2 = 8.f;
 constexpr uint64_t kWaitNs = 200000000ull;  // 200 ms: a healthy wait takes microseconds
 
+constexpr int kStages = 2;
+constexpr int kWarpsSoftmax = 8, kWarpProducer0 = 8, kWarpMma = 12;
+constexpr int kThreads = 13 * 32;
+
 struct PrefillSmem {
-	// each tile: two 64-column halves of 128 rows x 128 B, SW128
-	uint8_t q[kTileBytes];
-	uint8_t k[kTileBytes];
-	uint8_t v[kTileBytes];
-	uint8_t p[kTileBytes];    // P rounded to bf16
-	uint8_t pl[kTileBytes];   // P - bf16(P), rounded to bf16
-	uint64_t tma_bar, s_bar, pv_bar;
+	// tiles: two 64-column halves of 128 rows x 128 B, SW128
+	uint8_t q[2][kTileBytes];
+	uint8_t k[kStages][kTileBytes];
+	uint8_t v[kStages][kTileBytes];
+	uint64_t q_full;
+	uint64_t kv_full[kStages], kv_empty[kStages];
+	uint64_t s_full[2], p_full[2], o_full[2];
+	uint64_t drain;
 	uint32_t tmem_base;
-	int wait_ok;
-	uint32_t key_ok[kKeys / 32];
+	int abort;
+	int prod_ok[2];      // producer go / stop, double-buffered by block parity
+	uint32_t key_ok[kStages][kKeys / 32];
 	uint32_t lut[260];   // 256 scale entries + dequant multiplier constants
 };
 
@@ -87,6 +99,17 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
 		     "setp.ne.b32 p, %4, 0;\n\t"
 		     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
 		     :: "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Same, with A read from tensor memory (M = 128 rows in lanes 0..127, K
+// packed two bf16 per 32-bit column, the lower half first).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+					    uint32_t idesc, uint32_t accumulate)
+{
+	asm volatile("{\n\t.reg .pred p;\n\t"
+		     "setp.ne.b32 p, %4, 0;\n\t"
+		     "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+		     :: "r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t *bar)
@@ -217,289 +240,368 @@ __device__ __forceinline__ bool load_cached_row(const kllm_prefill_args &a, cons
 	return true;
 }
 
+// Bounded wait that gives up early once another role of the CTA aborted.
+__device__ __forceinline__ bool wait_or_abort(PrefillSmem &sm, uint64_t *bar, uint32_t parity,
+					      const kllm_prefill_args &a)
+{
+	if (mbar_try_wait(bar, parity))
+		return true;
+	const uint64_t t0 = global_ns();
+	for (;;) {
+		if (mbar_try_wait(bar, parity))
+			return true;
+		if (*reinterpret_cast<volatile int *>(&sm.abort))
+			return false;
+		if (global_ns() - t0 > kWaitNs) {
+			*reinterpret_cast<volatile int *>(&sm.abort) = 1;
+			if (a.err)
+				atomicOr(a.err, KLLM_ERR_TIMEOUT_BIT);
+			return false;
+		}
+	}
+}
+
+// Blocks of a tile whose last chunk position is `last` (-1: empty tile).
+__device__ __forceinline__ int tile_blocks(int n_prior, int last)
+{
+	return last < 0 ? 0 : n_prior + last / kKeys + 1;
+}
+
 template <int G>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __maxnreg__(128)
 prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm_k,
 	       const __grid_constant__ CUtensorMap tm_v)
 {
-	constexpr int BQ = kRows / G;  // chunk positions per CTA
+	constexpr int BQ = kRows / G;  // chunk positions per tile
 	extern __shared__ __align__(1024) uint8_t smem_raw[];
 	PrefillSmem &sm = *reinterpret_cast<PrefillSmem *>(
 	    (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
 
-	const int tid = threadIdx.x, warp = tid >> 5;
-	const int qb = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+	// the CTAs with the most key blocks (latest positions) start first
+	const int cb = gridDim.x - 1 - blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
 	const int t0 = a.cu_seqlens[seq];
 	const int clen = a.cu_seqlens[seq + 1] - t0;        // chunk length
 	const int ctx = max(a.ctx_lens[seq], 0);             // cached tokens before it
-	if (qb * BQ >= clen)
+	const int pos0 = cb * 2 * BQ;                        // first position, tile A
+	if (pos0 >= clen)
 		return;
+	if (a.err && (*reinterpret_cast<volatile uint32_t *>(a.err) & KLLM_ERR_TIMEOUT_BIT))
+		return;  // an earlier CTA timed out: the launch is already failed
 	const int ctx_cap = min(ctx, a.max_blocks * a.block_size);
+	const int n_prior = (ctx_cap + kKeys - 1) / kKeys;
+	const int nb_t[2] = {tile_blocks(n_prior, min(pos0 + BQ, clen) - 1),
+			     tile_blocks(n_prior, pos0 + BQ < clen ? min(pos0 + 2 * BQ, clen) - 1
+								   : -1)};
+	const int nb = max(nb_t[0], nb_t[1]);
 
-	// ---- setup: barriers, LUT, TMEM ----------------------------------------
+	// ---- setup ----------------------------------------------------------------
 	if (tid == 0) {
-		mbar_init(&sm.tma_bar, 1);
-		mbar_init(&sm.s_bar, 1);
-		mbar_init(&sm.pv_bar, 1);
+		mbar_init(&sm.q_full, 1);
+		for (int i = 0; i < kStages; ++i) {
+			mbar_init(&sm.kv_full[i], 1);
+			mbar_init(&sm.kv_empty[i], 1);
+		}
+		for (int t = 0; t < 2; ++t) {
+			mbar_init(&sm.s_full[t], 1);
+			mbar_init(&sm.p_full[t], 128);
+			mbar_init(&sm.o_full[t], 1);
+		}
+		mbar_init(&sm.drain, 1);
+		sm.abort = 0;
 		fence_mbar_init();
 	}
-	for (int i = tid; i < 256; i += 128)
+	for (int i = tid; i < 256; i += kThreads)
 		sm.lut[i] = mx_scale_lut_entry((uint32_t)i);
 	if (tid == 0) {
 		sm.lut[256] = 16u;
 		sm.lut[257] = 1u << 28;
 	}
-	if (warp == 0) {
+	if (warp == kWarpMma) {
 		asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-			     :: "r"(smem_u32(&sm.tmem_base)), "r"(256u));
+			     :: "r"(smem_u32(&sm.tmem_base)), "r"(512u));
 		asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
 	}
-
-	// ---- Q tile: row r = head h of the group, position p ------------------
-	const int h = tid / BQ, p = tid % BQ;          // this thread's row = tid
-	const int qpos = qb * BQ + p;                  // position inside the chunk
-	const bool row_live = qpos < clen;
-	{
-		uint32_t w[64];
-		if (row_live) {
-			const uint4 *src = reinterpret_cast<const uint4 *>(
-			    reinterpret_cast<const uint8_t *>(a.q) +
-			    (((size_t)(t0 + qpos) * a.num_heads + (size_t)kvh * G + h) * kD) * 2);
-#pragma unroll
-			for (int i = 0; i < 16; ++i) {
-				const uint4 v = src[i];
-				w[4 * i] = v.x;
-				w[4 * i + 1] = v.y;
-				w[4 * i + 2] = v.z;
-				w[4 * i + 3] = v.w;
-			}
-		} else {
-#pragma unroll
-			for (int i = 0; i < 64; ++i)
-				w[i] = 0u;
-		}
-		store_row(sm.q, tid, w);
-	}
-	fence_async_smem();
 	tc_fence_before();
 	__syncthreads();
 	tc_fence_after();
 	const uint32_t tmem = sm.tmem_base;
-	const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-	const uint32_t tS = t_lane, tO = t_lane + 128;
+	// TMEM columns: S_A 0, S_B 128, O_A 256, O_B 384
+	auto col_s = [](int t) { return (uint32_t)(t * 128); };
+	auto col_o = [](int t) { return (uint32_t)(256 + t * 128); };
 
-	// zero O in TMEM
-	{
-		float z[32];
-#pragma unroll
-		for (int i = 0; i < 32; ++i)
-			z[i] = 0.f;
-#pragma unroll
-		for (int c = 0; c < 4; ++c)
-			tmem_st32(tO + 32 * c, z);
-	}
-
-	const uint32_t sq = smem_u32(sm.q), sk = smem_u32(sm.k), sv = smem_u32(sm.v),
-		       sp = smem_u32(sm.p), spl = smem_u32(sm.pl);
-	const uint32_t id_s = umma_idesc(false), id_pv = umma_idesc(true);
-	float m_ref = -CUDART_INF_F, l_sum = 0.f;
-	bool ok = true;
-	uint32_t phase_s = 0, phase_pv = 0, phase_tma = 0;
-
-	const int n_prior = (ctx_cap + kKeys - 1) / kKeys;
-	const int last_q = min(qb * BQ + BQ, clen) - 1;    // last chunk position here
-	const int n_chunk = last_q / kKeys + 1;
-
-	for (int blk = 0; blk < n_prior + n_chunk && ok; ++blk) {
-		const bool prior = blk < n_prior;
-		const int kbase = prior ? blk * kKeys : (blk - n_prior) * kKeys;  // key offset
-		// ---- stage K and V -----------------------------------------------------
-		if (prior) {
-			uint32_t w[64];
-			const int kpos = kbase + tid;
-			bool live = kpos < ctx_cap;
-			bool okk = live && load_cached_row(a, sm.lut, seq, kvh, kpos, 0, w);
-			if (!okk) {
-#pragma unroll
-				for (int i = 0; i < 64; ++i)
-					w[i] = 0u;
+	if (warp < kWarpsSoftmax) {
+		// ================= softmax of tile t, row r ==============================
+		const int t = warp >> 2, r = (warp & 3) * 32 + lane;
+		const int h = r / BQ, p = r % BQ;
+		const int qpos = pos0 + t * BQ + p;               // position in the chunk
+		const bool row_live = qpos < clen;
+		const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+		const uint32_t tS = lane_base + col_s(t), tO = lane_base + col_o(t);
+		float m_ref = -CUDART_INF_F, l_sum = 0.f;
+		bool ok = true;
+		for (int j = 0; j < nb_t[t] && ok; ++j) {
+			// warp-uniform outcome: the TMEM accesses below are warp-collective
+			if (!__all_sync(0xffffffffu,
+					wait_or_abort(sm, &sm.s_full[t], (uint32_t)(j & 1), a))) {
+				ok = false;
+				break;
 			}
-			store_row(sm.k, tid, w);
-			if (okk)
-				load_cached_row(a, sm.lut, seq, kvh, kpos, 1, w);
-			store_row(sm.v, tid, w);
-			const uint32_t ball = __ballot_sync(0xffffffffu, okk);
-			if ((tid & 31) == 0)
-				sm.key_ok[warp] = ball;
-			fence_async_smem();
-		} else if (tid == 0) {
-			mbar_arrive_expect_tx(&sm.tma_bar, 4 * kHalfBytes);
-			const int y = t0 + kbase;
-			for (int half = 0; half < 2; ++half) {
-				tma_load_2d(sm.k + half * kHalfBytes, &tm_k, kvh * kD + half * kHalf, y, &sm.tma_bar);
-				tma_load_2d(sm.v + half * kHalfBytes, &tm_v, kvh * kD + half * kHalf, y, &sm.tma_bar);
+			tc_fence_after();
+			const bool prior = j < n_prior;
+			const int kbase = prior ? j * kKeys : (j - n_prior) * kKeys;
+			const float sl2 = a.scale_log2 * (prior && a.kv_dtype == 1 ? 256.f : 1.f);
+			const uint32_t *kok = sm.key_ok[j % kStages];
+			auto key_valid = [&](int jj) -> bool {
+				if (!row_live)
+					return false;
+				if (prior)
+					return (kok[jj >> 5] >> (jj & 31)) & 1u;
+				const int kp = kbase + jj;
+				return kp < clen && kp <= qpos;
+			};
+			float mx = -CUDART_INF_F;
+#pragma unroll
+			for (int c = 0; c < 4; ++c) {
+				float v[32];
+				tmem_ld32(tS + 32 * c, v);
+#pragma unroll
+				for (int i = 0; i < 32; ++i)
+					if (key_valid(32 * c + i))
+						mx = fmaxf(mx, v[i] * sl2);
 			}
-		}
-		if (!prior) {
-			if (tid == 0)
-				sm.wait_ok = mbar_wait_ns(&sm.tma_bar, phase_tma, kWaitNs);
-			phase_tma ^= 1u;
-		}
-		tc_fence_before();
-		__syncthreads();
-		if (!prior && !sm.wait_ok) {
-			ok = false;
-			break;
-		}
-		tc_fence_after();
-
-		// ---- S = Q K^T ---------------------------------------------------------
-		if (tid == 0) {
+			// raise the reference max when a row exceeds it by more than the
+			// slack; O holds data only after the first block (warp-uniform
+			// branch: tcgen05.ld/st are warp-collective)
+			const bool raise = mx > m_ref + kLazyLog2;
+			if (j > 0 && __any_sync(0xffffffffu, raise)) {
+				const float f = raise ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll
-			for (int kk = 0; kk < kD / 16; ++kk) {
-				const uint32_t off = (uint32_t)(kk >> 2) * kHalfBytes + (uint32_t)(kk & 3) * 32u;
-				umma_f16(tS, umma_desc(sq + off, 16u, 1024u), umma_desc(sk + off, 16u, 1024u),
-					 id_s, kk > 0);
+				for (int c = 0; c < 4; ++c) {
+					float v[32];
+					tmem_ld32(tO + 32 * c, v);
+#pragma unroll
+					for (int i = 0; i < 32; ++i)
+						v[i] *= f;
+					tmem_st32(tO + 32 * c, v);
+				}
 			}
-			umma_commit(&sm.s_bar);
-		}
-		if (tid == 0)
-			sm.wait_ok = mbar_wait_ns(&sm.s_bar, phase_s, kWaitNs);
-		phase_s ^= 1u;
-		__syncthreads();
-		if (!sm.wait_ok) {
-			ok = false;
-			break;
-		}
-		tc_fence_after();
-
-		// ---- softmax on this row ---------------------------------------------
-		// key j of the block is valid for this row when it exists and, for chunk
-		// keys, lies at or before the row's position (causal)
-		const float sl2 = a.scale_log2 * (prior && a.kv_dtype == 1 ? 256.f : 1.f);
-		auto key_valid = [&](int j) -> bool {
-			if (!row_live)
-				return false;
-			if (prior)
-				return (sm.key_ok[j >> 5] >> (j & 31)) & 1u;
-			const int kp = kbase + j;
-			return kp < clen && kp <= qpos;
-		};
-		float mx = -CUDART_INF_F;
+			if (raise) {
+				l_sum *= exp2f(m_ref - mx);
+				m_ref = mx;
+			}
+			const float pscale = prior && a.kv_dtype == 1 ? 256.f : 1.f;  // undo the V bias
 #pragma unroll
-		for (int c = 0; c < 4; ++c) {
-			float v[32];
-			tmem_ld32(tS + 32 * c, v);
+			for (int c = 0; c < 4; ++c) {
+				float v[32];
+				tmem_ld32(tS + 32 * c, v);
+				// keys 32c..32c+31 = 16-key groups 2c, 2c+1; group g occupies
+				// columns 16g..16g+7 (hi pairs) and 16g+8..16g+15 (lo pairs)
+				float w[32];
 #pragma unroll
-			for (int i = 0; i < 32; ++i)
-				if (key_valid(32 * c + i))
-					mx = fmaxf(mx, v[i] * sl2);
+				for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+					for (int i = 0; i < 8; ++i) {
+						const int j0 = 32 * c + 16 * gg + 2 * i;
+						const float p0 = key_valid(j0) ?
+						    exp2f(v[16 * gg + 2 * i] * sl2 - m_ref) : 0.f;
+						const float p1 = key_valid(j0 + 1) ?
+						    exp2f(v[16 * gg + 2 * i + 1] * sl2 - m_ref) : 0.f;
+						l_sum += p0 + p1;
+						const float q0 = p0 * pscale, q1 = p1 * pscale;
+						const uint32_t hi = pack_bf16x2(q0, q1);
+						const uint32_t lo = pack_bf16x2(q0 - __uint_as_float(hi << 16),
+										q1 - __uint_as_float(hi & 0xFFFF0000u));
+						w[16 * gg + i] = __uint_as_float(hi);
+						w[16 * gg + 8 + i] = __uint_as_float(lo);
+					}
+				tmem_st32(tS + 32 * c, w);
+			}
+			tc_fence_before();
+			mbar_arrive(&sm.p_full[t]);
 		}
-		// Raise the reference max where a row exceeds it by more than the
-		// slack. tcgen05.ld/st are warp-collective, so the O rescale runs for
-		// the whole warp when any of its rows needs it (factor 1 elsewhere).
-		const bool raise = mx > m_ref + kLazyLog2;
-		if (__any_sync(0xffffffffu, raise)) {
-			const float f = raise ? exp2f(m_ref - mx) : 1.f;
+		// ---- epilogue: O / l -> bf16 (every lane loads: warp-collective) ------
+		if (ok && nb_t[t] > 0 &&
+		    __all_sync(0xffffffffu, wait_or_abort(sm, &sm.o_full[t], 0u, a))) {
+			tc_fence_after();
+			const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+			uint4 *dst = reinterpret_cast<uint4 *>(
+			    reinterpret_cast<uint8_t *>(a.out) +
+			    (((size_t)(t0 + (row_live ? qpos : 0)) * a.num_heads + (size_t)kvh * G + h) *
+			     kD) * 2);
 #pragma unroll
 			for (int c = 0; c < 4; ++c) {
 				float v[32];
 				tmem_ld32(tO + 32 * c, v);
+				if (!row_live)
+					continue;
 #pragma unroll
-				for (int i = 0; i < 32; ++i)
-					v[i] *= f;
-				tmem_st32(tO + 32 * c, v);
-			}
-			if (raise) {
-				l_sum *= f;
-				m_ref = mx;
-			}
-		}
-		const float pscale = prior && a.kv_dtype == 1 ? 256.f : 1.f;  // undo the V bias
-#pragma unroll
-		for (int c = 0; c < 4; ++c) {
-			float v[32];
-			tmem_ld32(tS + 32 * c, v);
-			uint32_t pk[16], pr[16];
-#pragma unroll
-			for (int i = 0; i < 16; ++i) {
-				const int j0 = 32 * c + 2 * i;
-				const float p0 = key_valid(j0) ? exp2f(v[2 * i] * sl2 - m_ref) : 0.f;
-				const float p1 = key_valid(j0 + 1) ? exp2f(v[2 * i + 1] * sl2 - m_ref) : 0.f;
-				l_sum += p0 + p1;
-				const float q0 = p0 * pscale, q1 = p1 * pscale;
-				pk[i] = pack_bf16x2(q0, q1);
-				pr[i] = pack_bf16x2(q0 - __uint_as_float(pk[i] << 16),
-						    q1 - __uint_as_float(pk[i] & 0xFFFF0000u));
-			}
-			// keys 32c..32c+31 = half c/2, 16-byte chunks 4*(c%2) .. +3
-#pragma unroll
-			for (int j = 0; j < 4; ++j) {
-				const uint32_t off = (c >> 1) * kHalfBytes + sw128_offset(tid, 4 * (c & 1) + j);
-				*reinterpret_cast<uint4 *>(sm.p + off) =
-				    make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-				*reinterpret_cast<uint4 *>(sm.pl + off) =
-				    make_uint4(pr[4 * j], pr[4 * j + 1], pr[4 * j + 2], pr[4 * j + 3]);
+				for (int i = 0; i < 4; ++i)
+					dst[4 * c + i] = make_uint4(
+					    pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv),
+					    pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
+					    pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
+					    pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
 			}
 		}
-		fence_async_smem();
-		tc_fence_before();
-		__syncthreads();
-		tc_fence_after();
-
-		// ---- O += P V ------------------------------------------------------------
-		if (tid == 0) {
+	} else if (warp < kWarpMma) {
+		// ================= producer ==============================================
+		const int pt = tid - kWarpProducer0 * 32;          // 0..127: one row each
+		{
+			// Q rows of both tiles
+#pragma unroll 1
+			for (int t = 0; t < 2; ++t) {
+				const int h = pt / BQ, p = pt % BQ;
+				const int qpos = pos0 + t * BQ + p;
+				uint32_t w[64];
+				if (qpos < clen) {
+					const uint4 *src = reinterpret_cast<const uint4 *>(
+					    reinterpret_cast<const uint8_t *>(a.q) +
+					    (((size_t)(t0 + qpos) * a.num_heads + (size_t)kvh * G + h) * kD) * 2);
+#pragma unroll
+					for (int i = 0; i < 16; ++i) {
+						const uint4 v = src[i];
+						w[4 * i] = v.x;
+						w[4 * i + 1] = v.y;
+						w[4 * i + 2] = v.z;
+						w[4 * i + 3] = v.w;
+					}
+				} else {
+#pragma unroll
+					for (int i = 0; i < 64; ++i)
+						w[i] = 0u;
+				}
+				store_row(sm.q[t], pt, w);
+			}
+			fence_async_smem();
+			asm volatile("bar.sync 1, 128;" ::: "memory");
+			if (pt == 0)
+				mbar_arrive(&sm.q_full);
+		}
+		int issued_tma[kStages] = {-1, -1};   // last fill index armed by TMA, per stage
+		for (int j = 0; j < nb; ++j) {
+			const int st = j % kStages, fill = j / kStages;
+			// one thread waits for the stage; the group leaves together
+			if (pt == 0)
+				sm.prod_ok[j & 1] = fill == 0 ||
+				    wait_or_abort(sm, &sm.kv_empty[st], (uint32_t)((fill - 1) & 1), a);
+			asm volatile("bar.sync 1, 128;" ::: "memory");
+			if (!*reinterpret_cast<volatile int *>(&sm.prod_ok[j & 1]))
+				break;
+			if (j < n_prior) {
+				uint32_t w[64];
+				const int kpos = j * kKeys + pt;
+				const bool live = kpos < ctx_cap;
+				const bool okk = live && load_cached_row(a, sm.lut, seq, kvh, kpos, 0, w);
+				if (!okk) {
+#pragma unroll
+					for (int i = 0; i < 64; ++i)
+						w[i] = 0u;
+				}
+				store_row(sm.k[st], pt, w);
+				if (okk)
+					load_cached_row(a, sm.lut, seq, kvh, kpos, 1, w);
+				store_row(sm.v[st], pt, w);
+				const uint32_t ball = __ballot_sync(0xffffffffu, okk);
+				if (lane == 0)
+					sm.key_ok[st][pt >> 5] = ball;
+				fence_async_smem();
+				asm volatile("bar.sync 1, 128;" ::: "memory");
+				if (pt == 0)
+					mbar_arrive(&sm.kv_full[st]);
+			} else if (pt == 0) {
+				mbar_arrive_expect_tx(&sm.kv_full[st], 4 * kHalfBytes);
+				const int y = t0 + (j - n_prior) * kKeys;
+				for (int half = 0; half < 2; ++half) {
+					tma_load_2d(sm.k[st] + half * kHalfBytes, &tm_k, kvh * kD + half * kHalf, y,
+						    &sm.kv_full[st]);
+					tma_load_2d(sm.v[st] + half * kHalfBytes, &tm_v, kvh * kD + half * kHalf, y,
+						    &sm.kv_full[st]);
+				}
+				issued_tma[st] = fill;
+			}
+		}
+		// after an abort, wait (bounded) for this CTA's own tensor copies
+		if (pt == 0 && *reinterpret_cast<volatile int *>(&sm.abort))
+			for (int st = 0; st < kStages; ++st)
+				if (issued_tma[st] >= 0)
+					mbar_wait_ns(&sm.kv_full[st], (uint32_t)(issued_tma[st] & 1), kWaitNs);
+	} else if (lane == 0) {
+		// ================= MMA issue =============================================
+		const uint32_t id_s = umma_idesc(false), id_pv = umma_idesc(true);
+		const uint32_t sq[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
+		auto issue_s = [&](int t, int st) {
+			const uint32_t sk = smem_u32(sm.k[st]);
+#pragma unroll
+			for (int kk = 0; kk < kD / 16; ++kk) {
+				const uint32_t off = (uint32_t)(kk >> 2) * kHalfBytes + (uint32_t)(kk & 3) * 32u;
+				umma_f16(tmem + col_s(t), umma_desc(sq[t] + off, 16u, 1024u),
+					 umma_desc(sk + off, 16u, 1024u), id_s, kk > 0);
+			}
+		};
+		auto issue_pv = [&](int t, int st, bool first) {
+			const uint32_t sv = smem_u32(sm.v[st]);
 #pragma unroll
 			for (int kk = 0; kk < 2 * kKeys / 16; ++kk) {
-				const int k8 = kk & 7;   // kk < 8: P_hi, else P_lo
-				const uint32_t poff = (uint32_t)(k8 >> 2) * kHalfBytes + (uint32_t)(k8 & 3) * 32u;
-				const uint32_t voff = (uint32_t)k8 * 2048u;
-				umma_f16(tO, umma_desc((kk < 8 ? sp : spl) + poff, 16u, 1024u),
-					 umma_desc(sv + voff, (uint32_t)kHalfBytes, 1024u), id_pv, 1u);
+				const int g = kk >> 1;     // 16-key group; kk odd: the lo half of P
+				umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + 16u * g + 8u * (kk & 1),
+					    umma_desc(sv + (uint32_t)g * 2048u, (uint32_t)kHalfBytes, 1024u),
+					    id_pv, (first && kk == 0) ? 0u : 1u);
 			}
-			umma_commit(&sm.pv_bar);
+		};
+		bool ok = wait_or_abort(sm, &sm.q_full, 0u, a) &&
+			  wait_or_abort(sm, &sm.kv_full[0], 0u, a);
+		if (ok) {
+			tc_fence_after();
+			for (int t = 0; t < 2; ++t)
+				if (nb_t[t] > 0) {
+					issue_s(t, 0);
+					umma_commit(&sm.s_full[t]);
+				}
 		}
-		if (tid == 0)
-			sm.wait_ok = mbar_wait_ns(&sm.pv_bar, phase_pv, kWaitNs);
-		phase_pv ^= 1u;
-		__syncthreads();
-		if (!sm.wait_ok) {
-			ok = false;
-			break;
+		for (int j = 0; j < nb && ok; ++j) {
+			const int st = j % kStages;
+			for (int t = 0; t < 2 && ok; ++t) {
+				if (j < nb_t[t]) {
+					if (!wait_or_abort(sm, &sm.p_full[t], (uint32_t)(j & 1), a)) {
+						ok = false;
+						break;
+					}
+					tc_fence_after();
+					issue_pv(t, st, j == 0);
+				}
+				if (t == 0 && j + 1 < nb) {
+					// K/V of block j + 1 (for both tiles' next S)
+					if (!wait_or_abort(sm, &sm.kv_full[(j + 1) % kStages],
+							   (uint32_t)(((j + 1) / kStages) & 1), a)) {
+						ok = false;
+						break;
+					}
+					tc_fence_after();
+				}
+				if (j + 1 < nb_t[t]) {
+					issue_s(t, (j + 1) % kStages);
+					umma_commit(&sm.s_full[t]);
+				} else if (j + 1 == nb_t[t]) {
+					umma_commit(&sm.o_full[t]);
+				}
+			}
+			if (ok)
+				umma_commit(&sm.kv_empty[st]);
 		}
-		tc_fence_after();
+		// drain: every MMA issued by this thread completes before TMEM is freed
+		umma_commit(&sm.drain);
+		mbar_wait_ns(&sm.drain, 0u, kWaitNs);
 	}
 
-	// ---- epilogue: O / l -> bf16 ----------------------------------------------
-	// (every lane loads: tcgen05.ld is warp-collective; live rows store)
-	if (ok) {
-		const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-		uint4 *dst = reinterpret_cast<uint4 *>(
-		    reinterpret_cast<uint8_t *>(a.out) +
-		    (((size_t)(t0 + (row_live ? qpos : 0)) * a.num_heads + (size_t)kvh * G + h) *
-		     kD) * 2);
-#pragma unroll
-		for (int c = 0; c < 4; ++c) {
-			float v[32];
-			tmem_ld32(tO + 32 * c, v);
-			if (!row_live)
-				continue;
-#pragma unroll
-			for (int i = 0; i < 4; ++i)
-				dst[4 * c + i] = make_uint4(
-				    pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv),
-				    pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
-				    pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
-				    pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
-		}
-	} else if (tid == 0 && a.err) {
-		atomicOr(a.err, KLLM_ERR_TIMEOUT_BIT);
-	}
 	tc_fence_before();
 	__syncthreads();
-	if (warp == 0)
+	if (warp == kWarpMma) {
+		__syncwarp();
+		tc_fence_after();
 		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-			     :: "r"(tmem), "r"(256u));
+			     :: "r"(tmem), "r"(512u));
+	}
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode()
@@ -541,10 +643,27 @@ int launch_g(const kllm_prefill_args &a, const CUtensorMap &mk, const CUtensorMa
 					     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 	if (e != cudaSuccess)
 		return (int)e;
+	cudaFuncAttributes fa;
+	e = cudaFuncGetAttributes(&fa, prefill_kernel<G>);
+	if (e != cudaSuccess)
+		return (int)e;
 	constexpr int BQ = kRows / G;
-	dim3 grid((a.max_chunk + BQ - 1) / BQ, a.num_kv_heads, a.num_seqs);
-	prefill_kernel<G><<<grid, 128, smem, st>>>(a, mk, mv);
-	return (int)cudaGetLastError();
+	dim3 grid((a.max_chunk + 2 * BQ - 1) / (2 * BQ), a.num_kv_heads, a.num_seqs);
+	cudaError_t le = cudaSuccess;
+	if (fa.maxThreadsPerBlock < kThreads) {
+		le = cudaErrorLaunchOutOfResources;
+	} else {
+		prefill_kernel<G><<<grid, kThreads, smem, st>>>(a, mk, mv);
+		le = cudaGetLastError();
+	}
+	if (le != cudaSuccess && getenv("KLLM_GPU_DEBUG"))
+		fprintf(stderr,
+			"prefill_kernel<%d>: %s; regs %d, max threads %d, static smem %zu, "
+			"dynamic smem %zu (max %d), local %zu, grid %u x %u x %u x %d\n",
+			G, cudaGetErrorString(le), fa.numRegs, fa.maxThreadsPerBlock,
+			fa.sharedSizeBytes, smem, fa.maxDynamicSharedSizeBytes, fa.localSizeBytes,
+			grid.x, grid.y, grid.z, kThreads);
+	return (int)le;
 }
 
 }  // namespace

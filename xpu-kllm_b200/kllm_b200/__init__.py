@@ -78,7 +78,8 @@ class PrefillParams(Structure):
 
 class Stats(Structure):
     _fields_ = [("launches", c_uint64), ("kv_bytes", c_uint64), ("errors", c_uint64),
-                ("last_error", c_int), ("device", c_int), ("num_sms", c_int)]
+                ("last_error", c_int), ("device", c_int), ("num_sms", c_int),
+                ("last_cuda_error", c_int)]
 
 
 # (name, restype, argtypes) for every symbol include/kllm_gpu.h declares.
