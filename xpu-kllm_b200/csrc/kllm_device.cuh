@@ -53,6 +53,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
 	return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to hint_ns nanoseconds (it
+// resumes as soon as the phase completes), so a waiting warp costs almost no
+// issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity,
+						    uint32_t hint_ns)
+{
+	uint32_t ok;
+	asm volatile("{\n\t.reg .pred p;\n\t"
+		     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+		     "selp.u32 %0, 1, 0, p;\n\t}"
+		     : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+	return ok != 0;
+}
+
+// 2^x by the hardware approximation (relative error about 2^-22; results
+// below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2_approx(float x)
+{
+	float y;
+	asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+	return y;
+}
+
 // Bounded wait: each try_wait suspends for a hardware-bounded interval, so
 // kMaxTries bounds the wait to well under a minute. Returns false on expiry.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)

@@ -142,17 +142,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
 		v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
+// 16 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
 {
-	asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-		     "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-		     "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+	uint32_t r[16];
+	asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+		     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+		     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+		       "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+		       "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+		     : "r"(taddr));
+	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+	for (int i = 0; i < 16; ++i)
+		v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16])
+{
+	asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+		     "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
 		     :: "r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]),
 		        "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]),
-		        "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
-		        "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
-		        "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]),
-		        "f"(v[31])
+		        "f"(v[13]), "f"(v[14]), "f"(v[15])
 		     : "memory");
 	asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -173,44 +185,50 @@ struct DevEntry {
 	int pad;
 };
 
-// Writes one 128-element bf16 row (given as 64 packed words) into a tile.
-__device__ __forceinline__ void store_row(uint8_t *tile, int row, const uint32_t (&w)[64])
+// Writes half `half` (elements 64*half .. +63, as 32 packed words) of row
+// `row` into a tile: that half's 128-byte swizzled row.
+__device__ __forceinline__ void store_half_row(uint8_t *tile, int row, int half,
+					       const uint32_t (&w)[32])
 {
 #pragma unroll
-	for (int half = 0; half < 2; ++half)
-#pragma unroll
-		for (int c = 0; c < 8; ++c)
-			*reinterpret_cast<uint4 *>(tile + half * kHalfBytes + sw128_offset(row, c)) =
-			    make_uint4(w[half * 32 + c * 4], w[half * 32 + c * 4 + 1],
-				       w[half * 32 + c * 4 + 2], w[half * 32 + c * 4 + 3]);
+	for (int c = 0; c < 8; ++c)
+		*reinterpret_cast<uint4 *>(tile + half * kHalfBytes + sw128_offset(row, c)) =
+		    make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
-// One key row of the cached context (kv head kvh), as 128 exact bf16
-// values; zeros when the token has no valid page.
-__device__ __forceinline__ bool load_cached_row(const kllm_prefill_args &a, const uint32_t *lut,
-						int seq, int kvh, int kpos, int which,
-						uint32_t (&w)[64])
+// Page base (K if which == 0, else V) holding cached token kpos of the
+// sequence's kv head section, or null when the token has no valid page.
+__device__ __forceinline__ const uint8_t *cached_section(const kllm_prefill_args &a, int seq,
+							 int kvh, int kpos, int which, int &slot)
 {
 	const int bs = a.block_size;
-	const int page = kpos / bs, slot = kpos - page * bs;
+	const int page = kpos / bs;
+	slot = kpos - page * bs;
+	if (page >= a.max_blocks)
+		return nullptr;
 	const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
-			    (size_t)seq * a.max_blocks + (page < a.max_blocks ? page : 0);
+			    (size_t)seq * a.max_blocks + page;
 	const unsigned long long kp = e->k, vp = e->v;
-	if (page >= a.max_blocks || !e->valid || !kp) {
-#pragma unroll
-		for (int i = 0; i < 64; ++i)
-			w[i] = 0u;
-		return false;
-	}
-	const uint8_t *base = reinterpret_cast<const uint8_t *>(which ? vp : kp) + a.layer_off;
+	if (!e->valid || !kp)
+		return nullptr;
+	const size_t sec = a.kv_dtype == 1 ? (size_t)bs * kD * 9 / 8 : (size_t)bs * kD * 2;
+	return reinterpret_cast<const uint8_t *>(which ? vp : kp) + a.layer_off +
+	       (size_t)kvh * sec;
+}
+
+// Half `half` of one cached key/value row as 64 exact bf16 values (MX:
+// value x 2^-8, undone by the caller's scaling).
+__device__ __forceinline__ void load_cached_half(const kllm_prefill_args &a, const uint32_t *lut,
+						 const uint8_t *sec, int slot, int half,
+						 uint32_t (&w)[32])
+{
 	if (a.kv_dtype == 1) {
-		const size_t sec = (size_t)bs * kD * 9 / 8;
-		const uint8_t *pay = base + (size_t)kvh * sec + (size_t)slot * kD;
-		const uint8_t *scl = base + (size_t)kvh * sec + (size_t)bs * kD + (size_t)slot * (kD / 8);
-		const uint4 sc = *reinterpret_cast<const uint4 *>(scl);
-		const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
+		const uint8_t *pay = sec + (size_t)slot * kD + 64 * half;
+		const uint2 sc = *reinterpret_cast<const uint2 *>(
+		    sec + (size_t)a.block_size * kD + (size_t)slot * (kD / 8) + 8 * half);
+		const uint32_t scw[2] = {sc.x, sc.y};
 #pragma unroll
-		for (int i = 0; i < 8; ++i) {  // 16 payload bytes = 2 scale blocks
+		for (int i = 0; i < 4; ++i) {  // 16 payload bytes = 2 scale blocks
 			const uint4 pv = *reinterpret_cast<const uint4 *>(pay + 16 * i);
 			const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
@@ -219,17 +237,15 @@ __device__ __forceinline__ bool load_cached_row(const kllm_prefill_args &a, cons
 				const uint32_t s = lut[__byte_perm(scw[blk >> 2], 0u, 0x4440u | (blk & 3))];
 				uint32_t lo, hi;
 				e4m3x4_to_bf16x2_raw(pw[j], lut[256], lut[257], lo, hi);
-				// value * 2^-8 in bf16; exact, undone by scaling P by 2^8
 				w[8 * i + 2 * j] = bf16x2_mul(lo, s);
 				w[8 * i + 2 * j + 1] = bf16x2_mul(hi, s);
 			}
 		}
 	} else {
-		const size_t sec = (size_t)bs * kD * 2;
-		const uint4 *src = reinterpret_cast<const uint4 *>(base + (size_t)kvh * sec +
-								  (size_t)slot * kD * 2);
+		const uint4 *src = reinterpret_cast<const uint4 *>(sec + (size_t)slot * kD * 2 +
+								  128 * half);
 #pragma unroll
-		for (int i = 0; i < 16; ++i) {
+		for (int i = 0; i < 8; ++i) {
 			const uint4 v = src[i];
 			w[4 * i] = v.x;
 			w[4 * i + 1] = v.y;
@@ -237,7 +253,6 @@ __device__ __forceinline__ bool load_cached_row(const kllm_prefill_args &a, cons
 			w[4 * i + 3] = v.w;
 		}
 	}
-	return true;
 }
 
 // Bounded wait that gives up early once another role of the CTA aborted.
@@ -248,7 +263,7 @@ __device__ __forceinline__ bool wait_or_abort(PrefillSmem &sm, uint64_t *bar, ui
 		return true;
 	const uint64_t t0 = global_ns();
 	for (;;) {
-		if (mbar_try_wait(bar, parity))
+		if (mbar_try_wait_sleep(bar, parity, 20000u))
 			return true;
 		if (*reinterpret_cast<volatile int *>(&sm.abort))
 			return false;
@@ -351,25 +366,34 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			const bool prior = j < n_prior;
 			const int kbase = prior ? j * kKeys : (j - n_prior) * kKeys;
 			const float sl2 = a.scale_log2 * (prior && a.kv_dtype == 1 ? 256.f : 1.f);
-			const uint32_t *kok = sm.key_ok[j % kStages];
-			auto key_valid = [&](int jj) -> bool {
-				if (!row_live)
-					return false;
-				if (prior)
-					return (kok[jj >> 5] >> (jj & 31)) & 1u;
-				const int kp = kbase + jj;
-				return kp < clen && kp <= qpos;
-			};
-			float mx = -CUDART_INF_F;
+			// valid keys of this row in the block, 32 per word: cached keys
+			// with a page, or chunk keys at or before the row's position
+			uint32_t vmask[4];
+			{
+				const int lim = min(clen, qpos + 1) - kbase;   // chunk keys < lim
+#pragma unroll
+				for (int c = 0; c < 4; ++c) {
+					uint32_t mk;
+					if (prior)
+						mk = sm.key_ok[j % kStages][c];
+					else
+						mk = lim >= 32 * (c + 1) ? 0xFFFFFFFFu :
+						     (lim <= 32 * c ? 0u : (1u << (lim - 32 * c)) - 1u);
+					vmask[c] = row_live ? mk : 0u;
+				}
+			}
+			// max over raw scores (sl2 > 0), scaled once
+			float smax = -CUDART_INF_F;
 #pragma unroll
 			for (int c = 0; c < 4; ++c) {
 				float v[32];
 				tmem_ld32(tS + 32 * c, v);
 #pragma unroll
 				for (int i = 0; i < 32; ++i)
-					if (key_valid(32 * c + i))
-						mx = fmaxf(mx, v[i] * sl2);
+					if ((vmask[c] >> i) & 1u)
+						smax = fmaxf(smax, v[i]);
 			}
+			const float mx = smax * sl2;
 			// raise the reference max when a row exceeds it by more than the
 			// slack; O holds data only after the first block (warp-uniform
 			// branch: tcgen05.ld/st are warp-collective)
@@ -377,45 +401,44 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			if (j > 0 && __any_sync(0xffffffffu, raise)) {
 				const float f = raise ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll
-				for (int c = 0; c < 4; ++c) {
-					float v[32];
-					tmem_ld32(tO + 32 * c, v);
+				for (int c = 0; c < 8; ++c) {
+					float v[16];
+					tmem_ld16(tO + 16 * c, v);
 #pragma unroll
-					for (int i = 0; i < 32; ++i)
+					for (int i = 0; i < 16; ++i)
 						v[i] *= f;
-					tmem_st32(tO + 32 * c, v);
+					tmem_st16(tO + 16 * c, v);
 				}
 			}
 			if (raise) {
 				l_sum *= exp2f(m_ref - mx);
 				m_ref = mx;
 			}
+			const float moff = -m_ref;
 			const float pscale = prior && a.kv_dtype == 1 ? 256.f : 1.f;  // undo the V bias
+			// 16-key group g (keys 16g..16g+15, S columns 16g..16g+15) becomes
+			// P pairs: hi in columns 16g..16g+7, lo in 16g+8..16g+15
 #pragma unroll
-			for (int c = 0; c < 4; ++c) {
-				float v[32];
-				tmem_ld32(tS + 32 * c, v);
-				// keys 32c..32c+31 = 16-key groups 2c, 2c+1; group g occupies
-				// columns 16g..16g+7 (hi pairs) and 16g+8..16g+15 (lo pairs)
-				float w[32];
+			for (int g = 0; g < 8; ++g) {
+				float v[16];
+				tmem_ld16(tS + 16 * g, v);
+				const uint32_t gm = vmask[g >> 1] >> (16 * (g & 1));
+				float w[16];
 #pragma unroll
-				for (int gg = 0; gg < 2; ++gg)
-#pragma unroll
-					for (int i = 0; i < 8; ++i) {
-						const int j0 = 32 * c + 16 * gg + 2 * i;
-						const float p0 = key_valid(j0) ?
-						    exp2f(v[16 * gg + 2 * i] * sl2 - m_ref) : 0.f;
-						const float p1 = key_valid(j0 + 1) ?
-						    exp2f(v[16 * gg + 2 * i + 1] * sl2 - m_ref) : 0.f;
-						l_sum += p0 + p1;
-						const float q0 = p0 * pscale, q1 = p1 * pscale;
-						const uint32_t hi = pack_bf16x2(q0, q1);
-						const uint32_t lo = pack_bf16x2(q0 - __uint_as_float(hi << 16),
-										q1 - __uint_as_float(hi & 0xFFFF0000u));
-						w[16 * gg + i] = __uint_as_float(hi);
-						w[16 * gg + 8 + i] = __uint_as_float(lo);
-					}
-				tmem_st32(tS + 32 * c, w);
+				for (int i = 0; i < 8; ++i) {
+					const float p0 = ((gm >> (2 * i)) & 1u) ?
+					    ex2_approx(fmaf(v[2 * i], sl2, moff)) : 0.f;
+					const float p1 = ((gm >> (2 * i + 1)) & 1u) ?
+					    ex2_approx(fmaf(v[2 * i + 1], sl2, moff)) : 0.f;
+					l_sum += p0 + p1;
+					const float q0 = p0 * pscale, q1 = p1 * pscale;
+					const uint32_t hi = pack_bf16x2(q0, q1);
+					const uint32_t lo = pack_bf16x2(q0 - __uint_as_float(hi << 16),
+									q1 - __uint_as_float(hi & 0xFFFF0000u));
+					w[i] = __uint_as_float(hi);
+					w[8 + i] = __uint_as_float(lo);
+				}
+				tmem_st16(tS + 16 * g, w);
 			}
 			tc_fence_before();
 			mbar_arrive(&sm.p_full[t]);
@@ -430,14 +453,14 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			    (((size_t)(t0 + (row_live ? qpos : 0)) * a.num_heads + (size_t)kvh * G + h) *
 			     kD) * 2);
 #pragma unroll
-			for (int c = 0; c < 4; ++c) {
-				float v[32];
-				tmem_ld32(tO + 32 * c, v);
+			for (int c = 0; c < 8; ++c) {
+				float v[16];
+				tmem_ld16(tO + 16 * c, v);
 				if (!row_live)
 					continue;
 #pragma unroll
-				for (int i = 0; i < 4; ++i)
-					dst[4 * c + i] = make_uint4(
+				for (int i = 0; i < 2; ++i)
+					dst[2 * c + i] = make_uint4(
 					    pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv),
 					    pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
 					    pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
@@ -453,25 +476,23 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			for (int t = 0; t < 2; ++t) {
 				const int h = pt / BQ, p = pt % BQ;
 				const int qpos = pos0 + t * BQ + p;
-				uint32_t w[64];
-				if (qpos < clen) {
-					const uint4 *src = reinterpret_cast<const uint4 *>(
-					    reinterpret_cast<const uint8_t *>(a.q) +
-					    (((size_t)(t0 + qpos) * a.num_heads + (size_t)kvh * G + h) * kD) * 2);
+				const uint4 *src = reinterpret_cast<const uint4 *>(
+				    reinterpret_cast<const uint8_t *>(a.q) +
+				    (((size_t)(t0 + qpos) * a.num_heads + (size_t)kvh * G + h) * kD) * 2);
+#pragma unroll 1
+				for (int half = 0; half < 2; ++half) {
+					uint32_t w[32];
 #pragma unroll
-					for (int i = 0; i < 16; ++i) {
-						const uint4 v = src[i];
+					for (int i = 0; i < 8; ++i) {
+						const uint4 v = qpos < clen ? src[8 * half + i]
+									    : make_uint4(0u, 0u, 0u, 0u);
 						w[4 * i] = v.x;
 						w[4 * i + 1] = v.y;
 						w[4 * i + 2] = v.z;
 						w[4 * i + 3] = v.w;
 					}
-				} else {
-#pragma unroll
-					for (int i = 0; i < 64; ++i)
-						w[i] = 0u;
+					store_half_row(sm.q[t], pt, half, w);
 				}
-				store_row(sm.q[t], pt, w);
 			}
 			fence_async_smem();
 			asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -489,19 +510,27 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			if (!*reinterpret_cast<volatile int *>(&sm.prod_ok[j & 1]))
 				break;
 			if (j < n_prior) {
-				uint32_t w[64];
 				const int kpos = j * kKeys + pt;
-				const bool live = kpos < ctx_cap;
-				const bool okk = live && load_cached_row(a, sm.lut, seq, kvh, kpos, 0, w);
-				if (!okk) {
-#pragma unroll
-					for (int i = 0; i < 64; ++i)
-						w[i] = 0u;
+				int slot = 0;
+				const uint8_t *ks = nullptr, *vs = nullptr;
+				if (kpos < ctx_cap) {
+					ks = cached_section(a, seq, kvh, kpos, 0, slot);
+					vs = cached_section(a, seq, kvh, kpos, 1, slot);
 				}
-				store_row(sm.k[st], pt, w);
-				if (okk)
-					load_cached_row(a, sm.lut, seq, kvh, kpos, 1, w);
-				store_row(sm.v[st], pt, w);
+				const bool okk = ks != nullptr;
+#pragma unroll 1
+				for (int part = 0; part < 4; ++part) {   // K lo, K hi, V lo, V hi
+					uint32_t w[32];
+					const int half = part & 1;
+					if (okk) {
+						load_cached_half(a, sm.lut, part < 2 ? ks : vs, slot, half, w);
+					} else {
+#pragma unroll
+						for (int i = 0; i < 32; ++i)
+							w[i] = 0u;
+					}
+					store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+				}
 				const uint32_t ball = __ballot_sync(0xffffffffu, okk);
 				if (lane == 0)
 					sm.key_ok[st][pt >> 5] = ball;
