@@ -45,7 +45,11 @@ constexpr int kD = 128;             // head_dim
 constexpr int kHalf = 64;           // bf16 elements per 128-byte swizzle row
 constexpr int kTileBytes = kRows * kD * 2;    // 32 KB: one [128 x 128] bf16 tile
 constexpr int kHalfBytes = kTileBytes / 2;    // 16 KB: one 64-column half
-constexpr float kLazyLog2 = 8.f;
+// A row's reference max is raised only when a score exceeds it by more than
+// 2^kSlackLog2, so P <= 2^30 (x 2^8 on cached MX blocks): finite in bf16 and
+// in the fp32 accumulators, and the raise (a rescale of O, l and the P
+// already written) is rare after a row's first keys.
+constexpr float kSlackLog2 = 30.f;
 constexpr uint64_t kWaitNs = 200000000ull;  // 200 ms: a healthy wait takes microseconds
 
 constexpr int kStages = 2;
@@ -122,37 +126,53 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+// Issue-only forms: the caller waits (tcgen05.wait::ld / ::st) before using
+// the loaded registers / before signalling that the stores are visible.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16])
 {
-	uint32_t r[32];
-	asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-		     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-		     "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-		     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-		       "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-		       "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
-		       "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-		       "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-		       "=r"(r[30]), "=r"(r[31])
-		     : "r"(taddr));
-	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-	for (int i = 0; i < 32; ++i)
-		v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive fp32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
-{
-	uint32_t r[16];
 	asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
 		     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
 		     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
 		       "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
 		       "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-		     : "r"(taddr));
-	asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+		     : "r"(taddr) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const float (&v)[16])
+{
+	asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+		     "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+		     :: "r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]),
+		        "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]),
+		        "f"(v[13]), "f"(v[14]), "f"(v[15])
+		     : "memory");
+}
+
+// Waits for this thread's outstanding TMEM loads; the registers of a
+// prefetched load are in/out operands so that their uses follow the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16])
+{
+	asm volatile("tcgen05.wait::ld.sync.aligned;"
+		     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+		       "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+		       "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+		     :: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane. Load and wait are
+// one asm statement, so no use of the registers can be scheduled before the
+// wait.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+{
+	uint32_t r[16];
+	asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+		     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+		     "tcgen05.wait::ld.sync.aligned;"
+		     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+		       "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+		       "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+		     : "r"(taddr) : "memory");
 #pragma unroll
 	for (int i = 0; i < 16; ++i)
 		v[i] = __uint_as_float(r[i]);
@@ -282,6 +302,106 @@ __device__ __forceinline__ int tile_blocks(int n_prior, int last)
 	return last < 0 ? 0 : n_prior + last / kKeys + 1;
 }
 
+// p of one 16-key group -> bf16 hi/lo pairs: hi in w[0..7], lo in w[8..15]
+__device__ __forceinline__ void pack_p_pair(float q0, float q1, float &whi, float &wlo)
+{
+	const uint32_t hi = pack_bf16x2(q0, q1);
+	const uint32_t lo = pack_bf16x2(q0 - __uint_as_float(hi << 16),
+					q1 - __uint_as_float(hi & 0xFFFF0000u));
+	whi = __uint_as_float(hi);
+	wlo = __uint_as_float(lo);
+}
+
+// One 128-key block of one row: S (TMEM columns of tS) -> P written back in
+// place as 8 groups of (8 hi, 8 lo) bf16 pairs, p = 2^pexp x exp2(s x sl2 -
+// m_ref); l_sum gains sum(p) / 2^pexp. FULL: every key of every row of the
+// warp is valid (no mask). o_live: O already holds earlier blocks. Branches
+// around TMEM accesses are warp-uniform.
+template <bool FULL>
+__device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const uint32_t (&vmask)[4],
+					      float sl2, float pexp, bool o_live, float &m_ref,
+					      float &l_sum)
+{
+	float bsum = 0.f;
+	uint32_t nxt[16];
+	tmem_ld16_nowait(tS, nxt);
+#pragma unroll
+	for (int g = 0; g < 8; ++g) {
+		// group g's scores arrive; group g + 1's load overlaps this group's math
+		tmem_wait_ld(nxt);
+		float v[16];
+#pragma unroll
+		for (int i = 0; i < 16; ++i)
+			v[i] = __uint_as_float(nxt[i]);
+		if (g + 1 < 8)
+			tmem_ld16_nowait(tS + 16 * (g + 1), nxt);
+		const uint32_t gm = FULL ? 0xFFFFu : (vmask[g >> 1] >> (16 * (g & 1))) & 0xFFFFu;
+		float mv[16];
+#pragma unroll
+		for (int i = 0; i < 16; ++i)
+			mv[i] = (FULL || ((gm >> i) & 1u)) ? v[i] : -CUDART_INF_F;
+#pragma unroll
+		for (int w = 8; w >= 1; w >>= 1)     // tree max
+#pragma unroll
+			for (int i = 0; i < w; ++i)
+				mv[i] = fmaxf(mv[i], mv[i + w]);
+		const float gl = mv[0] * sl2;
+		const bool raise = gl > m_ref + kSlackLog2;
+		if (__any_sync(0xffffffffu, raise)) {
+			// rare: move the reference up, rescale what was built on the old one
+			// (group g + 1's prefetched scores in nxt stay valid: only O and
+			// the P groups before g change)
+			if (g + 1 < 8)
+				tmem_wait_ld(nxt);
+			tmem_wait_st();
+			const float f = raise ? exp2f(m_ref - gl) : 1.f;
+			if (o_live) {
+#pragma unroll 1
+				for (int c = 0; c < 8; ++c) {
+					float o[16];
+					tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+					for (int i = 0; i < 16; ++i)
+						o[i] *= f;
+					tmem_st16(tO + 16 * c, o);
+				}
+			}
+#pragma unroll 1
+			for (int gg = 0; gg < g; ++gg) {
+				float w[16];
+				tmem_ld16(tS + 16 * gg, w);
+#pragma unroll
+				for (int i = 0; i < 8; ++i) {
+					const uint32_t hi = __float_as_uint(w[i]), lo = __float_as_uint(w[8 + i]);
+					const float q0 = (__uint_as_float(hi << 16) + __uint_as_float(lo << 16)) * f;
+					const float q1 = (__uint_as_float(hi & 0xFFFF0000u) +
+							  __uint_as_float(lo & 0xFFFF0000u)) * f;
+					pack_p_pair(q0, q1, w[i], w[8 + i]);
+				}
+				tmem_st16(tS + 16 * gg, w);
+			}
+			bsum *= f;
+			l_sum *= f;
+			if (raise)
+				m_ref = gl;
+		}
+		const float moff = pexp - m_ref;
+		float w[16];
+#pragma unroll
+		for (int i = 0; i < 8; ++i) {
+			const float q0 = (FULL || ((gm >> (2 * i)) & 1u)) ?
+			    ex2_approx(fmaf(v[2 * i], sl2, moff)) : 0.f;
+			const float q1 = (FULL || ((gm >> (2 * i + 1)) & 1u)) ?
+			    ex2_approx(fmaf(v[2 * i + 1], sl2, moff)) : 0.f;
+			bsum += q0 + q1;
+			pack_p_pair(q0, q1, w[i], w[8 + i]);
+		}
+		tmem_st16_nowait(tS + 16 * g, w);
+	}
+	tmem_wait_st();
+	l_sum += bsum * exp2f(-pexp);
+}
+
 template <int G>
 __global__ void __maxnreg__(128)
 prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm_k,
@@ -382,64 +502,15 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					vmask[c] = row_live ? mk : 0u;
 				}
 			}
-			// max over raw scores (sl2 > 0), scaled once
-			float smax = -CUDART_INF_F;
-#pragma unroll
-			for (int c = 0; c < 4; ++c) {
-				float v[32];
-				tmem_ld32(tS + 32 * c, v);
-#pragma unroll
-				for (int i = 0; i < 32; ++i)
-					if ((vmask[c] >> i) & 1u)
-						smax = fmaxf(smax, v[i]);
-			}
-			const float mx = smax * sl2;
-			// raise the reference max when a row exceeds it by more than the
-			// slack; O holds data only after the first block (warp-uniform
-			// branch: tcgen05.ld/st are warp-collective)
-			const bool raise = mx > m_ref + kLazyLog2;
-			if (j > 0 && __any_sync(0xffffffffu, raise)) {
-				const float f = raise ? exp2f(m_ref - mx) : 1.f;
-#pragma unroll
-				for (int c = 0; c < 8; ++c) {
-					float v[16];
-					tmem_ld16(tO + 16 * c, v);
-#pragma unroll
-					for (int i = 0; i < 16; ++i)
-						v[i] *= f;
-					tmem_st16(tO + 16 * c, v);
-				}
-			}
-			if (raise) {
-				l_sum *= exp2f(m_ref - mx);
-				m_ref = mx;
-			}
-			const float moff = -m_ref;
-			const float pscale = prior && a.kv_dtype == 1 ? 256.f : 1.f;  // undo the V bias
-			// 16-key group g (keys 16g..16g+15, S columns 16g..16g+15) becomes
-			// P pairs: hi in columns 16g..16g+7, lo in 16g+8..16g+15
-#pragma unroll
-			for (int g = 0; g < 8; ++g) {
-				float v[16];
-				tmem_ld16(tS + 16 * g, v);
-				const uint32_t gm = vmask[g >> 1] >> (16 * (g & 1));
-				float w[16];
-#pragma unroll
-				for (int i = 0; i < 8; ++i) {
-					const float p0 = ((gm >> (2 * i)) & 1u) ?
-					    ex2_approx(fmaf(v[2 * i], sl2, moff)) : 0.f;
-					const float p1 = ((gm >> (2 * i + 1)) & 1u) ?
-					    ex2_approx(fmaf(v[2 * i + 1], sl2, moff)) : 0.f;
-					l_sum += p0 + p1;
-					const float q0 = p0 * pscale, q1 = p1 * pscale;
-					const uint32_t hi = pack_bf16x2(q0, q1);
-					const uint32_t lo = pack_bf16x2(q0 - __uint_as_float(hi << 16),
-									q1 - __uint_as_float(hi & 0xFFFF0000u));
-					w[i] = __uint_as_float(hi);
-					w[8 + i] = __uint_as_float(lo);
-				}
-				tmem_st16(tS + 16 * g, w);
-			}
+			// cached MX keys/values carry a 2^-8 factor: S is scaled back
+			// through sl2 and P is built 2^8 larger for the PV product
+			const float pexp = prior && a.kv_dtype == 1 ? 8.f : 0.f;
+			const bool full = __all_sync(0xffffffffu, (vmask[0] & vmask[1] & vmask[2] &
+								   vmask[3]) == 0xFFFFFFFFu);
+			if (full)
+				softmax_block<true>(tS, tO, vmask, sl2, pexp, j > 0, m_ref, l_sum);
+			else
+				softmax_block<false>(tS, tO, vmask, sl2, pexp, j > 0, m_ref, l_sum);
 			tc_fence_before();
 			mbar_arrive(&sm.p_full[t]);
 		}
