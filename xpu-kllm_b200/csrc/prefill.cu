@@ -10,8 +10,9 @@
 // 85-134) applied row by row with keys [0, position].
 //
 // One CTA per (sequence, kv head, 2 x 128/G chunk positions) holds two query
-// tiles A and B of 128 MMA rows each (row r = h * (128/G) + p: head h of the
-// group, position p), which share every K/V block. Per 128-key block j:
+// tiles A and B of 128 MMA rows each (row r = p * G + h: position p, head h
+// of the group, as a TMA box {64 dims, G heads, 128/G tokens} lands them),
+// which share every K/V block. Per 128-key block j:
 //   S_t = Q_t . K_j^T        tcgen05.mma kind::f16, Q and K in shared memory
 //   P_t = exp2(S_t*c - m)    one softmax thread per row (TMEM lane), written
 //                            back over S_t as bf16 hi + lo
@@ -50,6 +51,9 @@ constexpr int kHalfBytes = kTileBytes / 2;    // 16 KB: one 64-column half
 // in the fp32 accumulators, and the raise (a rescale of O, l and the P
 // already written) is rare after a row's first keys.
 constexpr float kSlackLog2 = 30.f;
+#ifndef KLLM_PF_WAIT_HINT
+#define KLLM_PF_WAIT_HINT 20000   // try_wait suspend hint, ns (0: plain try_wait)
+#endif
 constexpr uint64_t kWaitNs = 200000000ull;  // 200 ms: a healthy wait takes microseconds
 
 constexpr int kStages = 2;
@@ -62,7 +66,10 @@ struct PrefillSmem {
 	uint8_t k[kStages][kTileBytes];
 	uint8_t v[kStages][kTileBytes];
 	uint64_t q_full;
-	uint64_t kv_full[kStages], kv_empty[kStages];
+	// K and V stages fill and drain separately: K(j) is free once both tiles'
+	// S(j) are done, V(j) (and the key mask, read by the softmax of block j)
+	// once both PV(j) are issued after the softmax
+	uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
 	uint64_t s_full[2], p_full[2], o_full[2];
 	uint64_t drain;
 	uint32_t tmem_base;
@@ -148,16 +155,28 @@ __device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const float (&v
 		     : "memory");
 }
 
-// Waits for this thread's outstanding TMEM loads; the registers of a
-// prefetched load are in/out operands so that their uses follow the wait.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16])
+__device__ __forceinline__ void tmem_wait_ld4(uint32_t (&a)[16], uint32_t (&b)[16],
+					      uint32_t (&c)[16], uint32_t (&d)[16])
 {
+	// one wait for four prefetched loads; every register is an in/out operand
 	asm volatile("tcgen05.wait::ld.sync.aligned;"
-		     : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
-		       "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
-		       "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+		     : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+		       "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
+		       "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
+		       "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]),
+		       "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
+		       "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
+		     :: "memory");
+	asm volatile("tcgen05.wait::ld.sync.aligned;"
+		     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]), "+r"(c[4]), "+r"(c[5]),
+		       "+r"(c[6]), "+r"(c[7]), "+r"(c[8]), "+r"(c[9]), "+r"(c[10]), "+r"(c[11]),
+		       "+r"(c[12]), "+r"(c[13]), "+r"(c[14]), "+r"(c[15]),
+		       "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3]), "+r"(d[4]), "+r"(d[5]),
+		       "+r"(d[6]), "+r"(d[7]), "+r"(d[8]), "+r"(d[9]), "+r"(d[10]), "+r"(d[11]),
+		       "+r"(d[12]), "+r"(d[13]), "+r"(d[14]), "+r"(d[15])
 		     :: "memory");
 }
+
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 16 consecutive fp32 columns of this thread's TMEM lane. Load and wait are
@@ -199,6 +218,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 	    : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y,
+					    int z, uint64_t *bar)
+{
+	asm volatile(
+	    "cp.async.bulk.tensor.3d.shared::cta.global.mbarrier::complete_tx::bytes"
+	    " [%0], [%1, {%2, %3, %4}], [%5];"
+	    :: "r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+	    : "memory");
+}
+
 struct DevEntry {
 	unsigned long long k, v;
 	int valid;
@@ -234,6 +263,27 @@ __device__ __forceinline__ const uint8_t *cached_section(const kllm_prefill_args
 	const size_t sec = a.kv_dtype == 1 ? (size_t)bs * kD * 9 / 8 : (size_t)bs * kD * 2;
 	return reinterpret_cast<const uint8_t *>(which ? vp : kp) + a.layer_off +
 	       (size_t)kvh * sec;
+}
+
+// 64 MX elements (4 x 16 payload bytes, 8 scale bytes) -> 64 exact bf16
+// values x 2^-8, as 32 packed words.
+__device__ __forceinline__ void mx_dequant_half(const uint32_t *lut, const uint4 *pay, uint2 sc,
+						uint32_t (&w)[32])
+{
+	const uint32_t scw[2] = {sc.x, sc.y};
+#pragma unroll
+	for (int i = 0; i < 4; ++i) {  // 16 payload bytes = 2 scale blocks
+		const uint32_t pw[4] = {pay[i].x, pay[i].y, pay[i].z, pay[i].w};
+#pragma unroll
+		for (int j = 0; j < 4; ++j) {
+			const int blk = 2 * i + (j >> 1);
+			const uint32_t s = lut[__byte_perm(scw[blk >> 2], 0u, 0x4440u | (blk & 3))];
+			uint32_t lo, hi;
+			e4m3x4_to_bf16x2_raw(pw[j], lut[256], lut[257], lo, hi);
+			w[8 * i + 2 * j] = bf16x2_mul(lo, s);
+			w[8 * i + 2 * j + 1] = bf16x2_mul(hi, s);
+		}
+	}
 }
 
 // Half `half` of one cached key/value row as 64 exact bf16 values (MX:
@@ -282,9 +332,16 @@ __device__ __forceinline__ bool wait_or_abort(PrefillSmem &sm, uint64_t *bar, ui
 	if (mbar_try_wait(bar, parity))
 		return true;
 	const uint64_t t0 = global_ns();
-	for (;;) {
-		if (mbar_try_wait_sleep(bar, parity, 20000u))
+	for (uint32_t n = 0;; ++n) {
+#if KLLM_PF_WAIT_HINT > 0
+		if (mbar_try_wait_sleep(bar, parity, KLLM_PF_WAIT_HINT))
 			return true;
+#else
+		if (mbar_try_wait(bar, parity))
+			return true;
+		if (n & 31u)
+			continue;   // the clock and the abort flag every 32 tries
+#endif
 		if (*reinterpret_cast<volatile int *>(&sm.abort))
 			return false;
 		if (global_ns() - t0 > kWaitNs) {
@@ -317,31 +374,73 @@ __device__ __forceinline__ void pack_p_pair(float q0, float q1, float &whi, floa
 // m_ref); l_sum gains sum(p) / 2^pexp. FULL: every key of every row of the
 // warp is valid (no mask). o_live: O already holds earlier blocks. Branches
 // around TMEM accesses are warp-uniform.
+// Multiplies this row's O (when o_live) and its first n_groups P groups of
+// the current block by f (warp-collective: the whole warp calls it; rare).
+__device__ __forceinline__ void rescale_row(uint32_t tS, uint32_t tO, float f, bool o_live,
+					 int n_groups)
+{
+	tmem_wait_st();
+	if (o_live) {
+#pragma unroll 1
+		for (int c = 0; c < 8; ++c) {
+			float o[16];
+			tmem_ld16(tO + 16 * c, o);
+#pragma unroll
+			for (int i = 0; i < 16; ++i)
+				o[i] *= f;
+			tmem_st16(tO + 16 * c, o);
+		}
+	}
+#pragma unroll 1
+	for (int gg = 0; gg < n_groups; ++gg) {
+		float w[16];
+		tmem_ld16(tS + 16 * gg, w);
+#pragma unroll
+		for (int i = 0; i < 8; ++i) {
+			const uint32_t hi = __float_as_uint(w[i]), lo = __float_as_uint(w[8 + i]);
+			const float q0 = (__uint_as_float(hi << 16) + __uint_as_float(lo << 16)) * f;
+			const float q1 = (__uint_as_float(hi & 0xFFFF0000u) +
+					  __uint_as_float(lo & 0xFFFF0000u)) * f;
+			pack_p_pair(q0, q1, w[i], w[8 + i]);
+		}
+		tmem_st16(tS + 16 * gg, w);
+	}
+}
+
 template <bool FULL>
 __device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const uint32_t (&vmask)[4],
 					      float sl2, float pexp, bool o_live, float &m_ref,
 					      float &l_sum)
 {
 	float bsum = 0.f;
-	uint32_t nxt[16];
-	tmem_ld16_nowait(tS, nxt);
+	// two halves of 64 keys: four 16-column loads in flight, one max tree and
+	// one warp vote per half
 #pragma unroll
-	for (int g = 0; g < 8; ++g) {
-		// group g's scores arrive; group g + 1's load overlaps this group's math
-		tmem_wait_ld(nxt);
-		float v[16];
+	for (int hb = 0; hb < 2; ++hb) {
+		uint32_t r0[16], r1[16], r2[16], r3[16];
+		tmem_ld16_nowait(tS + 64 * hb, r0);
+		tmem_ld16_nowait(tS + 64 * hb + 16, r1);
+		tmem_ld16_nowait(tS + 64 * hb + 32, r2);
+		tmem_ld16_nowait(tS + 64 * hb + 48, r3);
+		tmem_wait_ld4(r0, r1, r2, r3);
+		float v[64];
 #pragma unroll
-		for (int i = 0; i < 16; ++i)
-			v[i] = __uint_as_float(nxt[i]);
-		if (g + 1 < 8)
-			tmem_ld16_nowait(tS + 16 * (g + 1), nxt);
-		const uint32_t gm = FULL ? 0xFFFFu : (vmask[g >> 1] >> (16 * (g & 1))) & 0xFFFFu;
-		float mv[16];
+		for (int i = 0; i < 16; ++i) {
+			v[i] = __uint_as_float(r0[i]);
+			v[16 + i] = __uint_as_float(r1[i]);
+			v[32 + i] = __uint_as_float(r2[i]);
+			v[48 + i] = __uint_as_float(r3[i]);
+		}
+		const uint32_t m0 = FULL ? 0xFFFFFFFFu : vmask[2 * hb], m1 = FULL ? 0xFFFFFFFFu : vmask[2 * hb + 1];
+		auto valid = [&](int i) -> bool {
+			return FULL || (((i < 32 ? m0 : m1) >> (i & 31)) & 1u);
+		};
+		float mv[32];
 #pragma unroll
-		for (int i = 0; i < 16; ++i)
-			mv[i] = (FULL || ((gm >> i) & 1u)) ? v[i] : -CUDART_INF_F;
+		for (int i = 0; i < 32; ++i)
+			mv[i] = fmaxf(valid(i) ? v[i] : -CUDART_INF_F, valid(32 + i) ? v[32 + i] : -CUDART_INF_F);
 #pragma unroll
-		for (int w = 8; w >= 1; w >>= 1)     // tree max
+		for (int w = 16; w >= 1; w >>= 1)     // tree max
 #pragma unroll
 			for (int i = 0; i < w; ++i)
 				mv[i] = fmaxf(mv[i], mv[i + w]);
@@ -349,54 +448,28 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const ui
 		const bool raise = gl > m_ref + kSlackLog2;
 		if (__any_sync(0xffffffffu, raise)) {
 			// rare: move the reference up, rescale what was built on the old one
-			// (group g + 1's prefetched scores in nxt stay valid: only O and
-			// the P groups before g change)
-			if (g + 1 < 8)
-				tmem_wait_ld(nxt);
-			tmem_wait_st();
 			const float f = raise ? exp2f(m_ref - gl) : 1.f;
-			if (o_live) {
-#pragma unroll 1
-				for (int c = 0; c < 8; ++c) {
-					float o[16];
-					tmem_ld16(tO + 16 * c, o);
-#pragma unroll
-					for (int i = 0; i < 16; ++i)
-						o[i] *= f;
-					tmem_st16(tO + 16 * c, o);
-				}
-			}
-#pragma unroll 1
-			for (int gg = 0; gg < g; ++gg) {
-				float w[16];
-				tmem_ld16(tS + 16 * gg, w);
-#pragma unroll
-				for (int i = 0; i < 8; ++i) {
-					const uint32_t hi = __float_as_uint(w[i]), lo = __float_as_uint(w[8 + i]);
-					const float q0 = (__uint_as_float(hi << 16) + __uint_as_float(lo << 16)) * f;
-					const float q1 = (__uint_as_float(hi & 0xFFFF0000u) +
-							  __uint_as_float(lo & 0xFFFF0000u)) * f;
-					pack_p_pair(q0, q1, w[i], w[8 + i]);
-				}
-				tmem_st16(tS + 16 * gg, w);
-			}
+			rescale_row(tS, tO, f, o_live, 4 * hb);
 			bsum *= f;
 			l_sum *= f;
 			if (raise)
 				m_ref = gl;
 		}
 		const float moff = pexp - m_ref;
-		float w[16];
+		// 16-key group g of this half -> 8 hi pairs, then 8 lo pairs
 #pragma unroll
-		for (int i = 0; i < 8; ++i) {
-			const float q0 = (FULL || ((gm >> (2 * i)) & 1u)) ?
-			    ex2_approx(fmaf(v[2 * i], sl2, moff)) : 0.f;
-			const float q1 = (FULL || ((gm >> (2 * i + 1)) & 1u)) ?
-			    ex2_approx(fmaf(v[2 * i + 1], sl2, moff)) : 0.f;
-			bsum += q0 + q1;
-			pack_p_pair(q0, q1, w[i], w[8 + i]);
+		for (int g = 0; g < 4; ++g) {
+			float w[16];
+#pragma unroll
+			for (int i = 0; i < 8; ++i) {
+				const int k0 = 16 * g + 2 * i;
+				const float q0 = valid(k0) ? ex2_approx(fmaf(v[k0], sl2, moff)) : 0.f;
+				const float q1 = valid(k0 + 1) ? ex2_approx(fmaf(v[k0 + 1], sl2, moff)) : 0.f;
+				bsum += q0 + q1;
+				pack_p_pair(q0, q1, w[i], w[8 + i]);
+			}
+			tmem_st16_nowait(tS + 64 * hb + 16 * g, w);
 		}
-		tmem_st16_nowait(tS + 16 * g, w);
 	}
 	tmem_wait_st();
 	l_sum += bsum * exp2f(-pexp);
@@ -404,8 +477,8 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const ui
 
 template <int G>
 __global__ void __maxnreg__(128)
-prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm_k,
-	       const __grid_constant__ CUtensorMap tm_v)
+prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm_q,
+	       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v)
 {
 	constexpr int BQ = kRows / G;  // chunk positions per tile
 	extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -434,8 +507,10 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 	if (tid == 0) {
 		mbar_init(&sm.q_full, 1);
 		for (int i = 0; i < kStages; ++i) {
-			mbar_init(&sm.kv_full[i], 1);
-			mbar_init(&sm.kv_empty[i], 1);
+			mbar_init(&sm.k_full[i], 1);
+			mbar_init(&sm.k_empty[i], 1);
+			mbar_init(&sm.v_full[i], 1);
+			mbar_init(&sm.v_empty[i], 1);
 		}
 		for (int t = 0; t < 2; ++t) {
 			mbar_init(&sm.s_full[t], 1);
@@ -468,7 +543,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 	if (warp < kWarpsSoftmax) {
 		// ================= softmax of tile t, row r ==============================
 		const int t = warp >> 2, r = (warp & 3) * 32 + lane;
-		const int h = r / BQ, p = r % BQ;
+		const int h = r % G, p = r / G;
 		const int qpos = pos0 + t * BQ + p;               // position in the chunk
 		const bool row_live = qpos < clen;
 		const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
@@ -541,46 +616,31 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 	} else if (warp < kWarpMma) {
 		// ================= producer ==============================================
 		const int pt = tid - kWarpProducer0 * 32;          // 0..127: one row each
-		{
-			// Q rows of both tiles
-#pragma unroll 1
-			for (int t = 0; t < 2; ++t) {
-				const int h = pt / BQ, p = pt % BQ;
-				const int qpos = pos0 + t * BQ + p;
-				const uint4 *src = reinterpret_cast<const uint4 *>(
-				    reinterpret_cast<const uint8_t *>(a.q) +
-				    (((size_t)(t0 + qpos) * a.num_heads + (size_t)kvh * G + h) * kD) * 2);
-#pragma unroll 1
-				for (int half = 0; half < 2; ++half) {
-					uint32_t w[32];
-#pragma unroll
-					for (int i = 0; i < 8; ++i) {
-						const uint4 v = qpos < clen ? src[8 * half + i]
-									    : make_uint4(0u, 0u, 0u, 0u);
-						w[4 * i] = v.x;
-						w[4 * i + 1] = v.y;
-						w[4 * i + 2] = v.z;
-						w[4 * i + 3] = v.w;
-					}
-					store_half_row(sm.q[t], pt, half, w);
-				}
-			}
-			fence_async_smem();
-			asm volatile("bar.sync 1, 128;" ::: "memory");
-			if (pt == 0)
-				mbar_arrive(&sm.q_full);
+		if (pt == 0) {
+			// both query tiles by TMA: box {64 dims, G heads, BQ tokens} per half
+			mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
+			for (int t = 0; t < 2; ++t)
+				for (int half = 0; half < 2; ++half)
+					tma_load_3d(sm.q[t] + half * kHalfBytes, &tm_q, half * kHalf, kvh * G,
+						    t0 + pos0 + t * BQ, &sm.q_full);
 		}
-		int issued_tma[kStages] = {-1, -1};   // last fill index armed by TMA, per stage
+		int issued_k[kStages] = {-1, -1}, issued_v[kStages] = {-1, -1};  // TMA fills armed
+		bool alive = true;   // thread 0: no wait of its own has failed
 		for (int j = 0; j < nb; ++j) {
 			const int st = j % kStages, fill = j / kStages;
+			const uint32_t par = (uint32_t)((fill - 1) & 1);
+			const bool prior = j < n_prior;
 			// one thread waits for the stage; the group leaves together
-			if (pt == 0)
-				sm.prod_ok[j & 1] = fill == 0 ||
-				    wait_or_abort(sm, &sm.kv_empty[st], (uint32_t)((fill - 1) & 1), a);
+			if (pt == 0) {
+				bool okw = alive && (fill == 0 || wait_or_abort(sm, &sm.k_empty[st], par, a));
+				if (okw && prior)   // the dequant writes K and V (and the key mask) at once
+					okw = fill == 0 || wait_or_abort(sm, &sm.v_empty[st], par, a);
+				sm.prod_ok[j & 1] = okw;
+			}
 			asm volatile("bar.sync 1, 128;" ::: "memory");
 			if (!*reinterpret_cast<volatile int *>(&sm.prod_ok[j & 1]))
 				break;
-			if (j < n_prior) {
+			if (prior) {
 				const int kpos = j * kKeys + pt;
 				int slot = 0;
 				const uint8_t *ks = nullptr, *vs = nullptr;
@@ -589,43 +649,87 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					vs = cached_section(a, seq, kvh, kpos, 1, slot);
 				}
 				const bool okk = ks != nullptr;
-#pragma unroll 1
-				for (int part = 0; part < 4; ++part) {   // K lo, K hi, V lo, V hi
-					uint32_t w[32];
-					const int half = part & 1;
+				if (a.kv_dtype == 1) {
+					// K and V rows (payload + scales) all in flight, then convert
+					uint4 kpay[8], vpay[8], ksc, vsc;
 					if (okk) {
-						load_cached_half(a, sm.lut, part < 2 ? ks : vs, slot, half, w);
+						const uint4 *kq = reinterpret_cast<const uint4 *>(ks + (size_t)slot * kD);
+						const uint4 *vq = reinterpret_cast<const uint4 *>(vs + (size_t)slot * kD);
+#pragma unroll
+						for (int i = 0; i < 8; ++i) {
+							kpay[i] = kq[i];
+							vpay[i] = vq[i];
+						}
+						const size_t so = (size_t)a.block_size * kD + (size_t)slot * (kD / 8);
+						ksc = *reinterpret_cast<const uint4 *>(ks + so);
+						vsc = *reinterpret_cast<const uint4 *>(vs + so);
 					} else {
 #pragma unroll
-						for (int i = 0; i < 32; ++i)
-							w[i] = 0u;
+						for (int i = 0; i < 8; ++i)
+							kpay[i] = vpay[i] = make_uint4(0u, 0u, 0u, 0u);
+						ksc = vsc = make_uint4(0u, 0u, 0u, 0u);
 					}
-					store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+#pragma unroll
+					for (int part = 0; part < 4; ++part) {   // K lo, K hi, V lo, V hi
+						const int half = part & 1;
+						const uint4 *pay = part < 2 ? kpay : vpay;
+						const uint4 sc = part < 2 ? ksc : vsc;
+						uint32_t w[32];
+						mx_dequant_half(sm.lut, pay + 4 * half,
+								half ? make_uint2(sc.z, sc.w) : make_uint2(sc.x, sc.y), w);
+						store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+					}
+				} else {
+#pragma unroll 1
+					for (int part = 0; part < 4; ++part) {   // K lo, K hi, V lo, V hi
+						uint32_t w[32];
+						const int half = part & 1;
+						if (okk) {
+							load_cached_half(a, sm.lut, part < 2 ? ks : vs, slot, half, w);
+						} else {
+#pragma unroll
+							for (int i = 0; i < 32; ++i)
+								w[i] = 0u;
+						}
+						store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+					}
 				}
 				const uint32_t ball = __ballot_sync(0xffffffffu, okk);
 				if (lane == 0)
 					sm.key_ok[st][pt >> 5] = ball;
 				fence_async_smem();
 				asm volatile("bar.sync 1, 128;" ::: "memory");
-				if (pt == 0)
-					mbar_arrive(&sm.kv_full[st]);
-			} else if (pt == 0) {
-				mbar_arrive_expect_tx(&sm.kv_full[st], 4 * kHalfBytes);
-				const int y = t0 + (j - n_prior) * kKeys;
-				for (int half = 0; half < 2; ++half) {
-					tma_load_2d(sm.k[st] + half * kHalfBytes, &tm_k, kvh * kD + half * kHalf, y,
-						    &sm.kv_full[st]);
-					tma_load_2d(sm.v[st] + half * kHalfBytes, &tm_v, kvh * kD + half * kHalf, y,
-						    &sm.kv_full[st]);
+				if (pt == 0) {
+					mbar_arrive(&sm.k_full[st]);
+					mbar_arrive(&sm.v_full[st]);
 				}
-				issued_tma[st] = fill;
+			} else if (pt == 0) {
+				const int y = t0 + (j - n_prior) * kKeys;
+				mbar_arrive_expect_tx(&sm.k_full[st], 2 * kHalfBytes);
+				for (int half = 0; half < 2; ++half)
+					tma_load_2d(sm.k[st] + half * kHalfBytes, &tm_k, kvh * kD + half * kHalf, y,
+						    &sm.k_full[st]);
+				issued_k[st] = fill;
+				alive = fill == 0 || wait_or_abort(sm, &sm.v_empty[st], par, a);
+				if (alive) {
+					mbar_arrive_expect_tx(&sm.v_full[st], 2 * kHalfBytes);
+					for (int half = 0; half < 2; ++half)
+						tma_load_2d(sm.v[st] + half * kHalfBytes, &tm_v, kvh * kD + half * kHalf,
+							    y, &sm.v_full[st]);
+					issued_v[st] = fill;
+				}
 			}
 		}
 		// after an abort, wait (bounded) for this CTA's own tensor copies
-		if (pt == 0 && *reinterpret_cast<volatile int *>(&sm.abort))
-			for (int st = 0; st < kStages; ++st)
-				if (issued_tma[st] >= 0)
-					mbar_wait_ns(&sm.kv_full[st], (uint32_t)(issued_tma[st] & 1), kWaitNs);
+		if (pt == 0 && *reinterpret_cast<volatile int *>(&sm.abort)) {
+			mbar_wait_ns(&sm.q_full, 0u, kWaitNs);
+			for (int st = 0; st < kStages; ++st) {
+				if (issued_k[st] >= 0)
+					mbar_wait_ns(&sm.k_full[st], (uint32_t)(issued_k[st] & 1), kWaitNs);
+				if (issued_v[st] >= 0)
+					mbar_wait_ns(&sm.v_full[st], (uint32_t)(issued_v[st] & 1), kWaitNs);
+			}
+		}
 	} else if (lane == 0) {
 		// ================= MMA issue =============================================
 		const uint32_t id_s = umma_idesc(false), id_pv = umma_idesc(true);
@@ -650,7 +754,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			}
 		};
 		bool ok = wait_or_abort(sm, &sm.q_full, 0u, a) &&
-			  wait_or_abort(sm, &sm.kv_full[0], 0u, a);
+			  wait_or_abort(sm, &sm.k_full[0], 0u, a);
 		if (ok) {
 			tc_fence_after();
 			for (int t = 0; t < 2; ++t)
@@ -658,9 +762,11 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					issue_s(t, 0);
 					umma_commit(&sm.s_full[t]);
 				}
+			umma_commit(&sm.k_empty[0]);
 		}
 		for (int j = 0; j < nb && ok; ++j) {
-			const int st = j % kStages;
+			const int st = j % kStages, ns = (j + 1) % kStages;
+			ok = wait_or_abort(sm, &sm.v_full[st], (uint32_t)((j / kStages) & 1), a);
 			for (int t = 0; t < 2 && ok; ++t) {
 				if (j < nb_t[t]) {
 					if (!wait_or_abort(sm, &sm.p_full[t], (uint32_t)(j & 1), a)) {
@@ -670,24 +776,26 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					tc_fence_after();
 					issue_pv(t, st, j == 0);
 				}
+				if (t == 1)
+					umma_commit(&sm.v_empty[st]);   // both PV(j) issued: V(j) free when done
 				if (t == 0 && j + 1 < nb) {
-					// K/V of block j + 1 (for both tiles' next S)
-					if (!wait_or_abort(sm, &sm.kv_full[(j + 1) % kStages],
-							   (uint32_t)(((j + 1) / kStages) & 1), a)) {
+					// K of block j + 1, for both tiles' next S
+					if (!wait_or_abort(sm, &sm.k_full[ns], (uint32_t)(((j + 1) / kStages) & 1),
+							   a)) {
 						ok = false;
 						break;
 					}
 					tc_fence_after();
 				}
 				if (j + 1 < nb_t[t]) {
-					issue_s(t, (j + 1) % kStages);
+					issue_s(t, ns);
 					umma_commit(&sm.s_full[t]);
 				} else if (j + 1 == nb_t[t]) {
 					umma_commit(&sm.o_full[t]);
 				}
 			}
-			if (ok)
-				umma_commit(&sm.kv_empty[st]);
+			if (ok && j + 1 < nb)
+				umma_commit(&sm.k_empty[ns]);       // both S(j + 1) issued
 		}
 		// drain: every MMA issued by this thread completes before TMEM is freed
 		umma_commit(&sm.drain);
@@ -734,8 +842,26 @@ bool make_map(CUtensorMap *m, const void *base, int num_tokens, int hkv)
 		   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [num_tokens][num_heads][128] bf16 as {dims, heads, tokens}, box 64 dims x
+// G heads x 128/G tokens (one 128-row half tile), 128-byte swizzle
+bool make_q_map(CUtensorMap *m, const void *base, int num_tokens, int hq, int g)
+{
+	auto enc = get_encode();
+	if (!enc)
+		return false;
+	cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)hq, (cuuint64_t)num_tokens};
+	cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)hq * kD * 2};
+	cuuint32_t box[3] = {(cuuint32_t)kHalf, (cuuint32_t)g, (cuuint32_t)(kRows / g)};
+	cuuint32_t estr[3] = {1, 1, 1};
+	return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+		   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+		   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+		   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int G>
-int launch_g(const kllm_prefill_args &a, const CUtensorMap &mk, const CUtensorMap &mv,
+int launch_g(const kllm_prefill_args &a, const CUtensorMap &mq, const CUtensorMap &mk,
+	     const CUtensorMap &mv,
 	     cudaStream_t st)
 {
 	const size_t smem = sizeof(PrefillSmem) + 1024;
@@ -753,7 +879,7 @@ int launch_g(const kllm_prefill_args &a, const CUtensorMap &mk, const CUtensorMa
 	if (fa.maxThreadsPerBlock < kThreads) {
 		le = cudaErrorLaunchOutOfResources;
 	} else {
-		prefill_kernel<G><<<grid, kThreads, smem, st>>>(a, mk, mv);
+		prefill_kernel<G><<<grid, kThreads, smem, st>>>(a, mq, mk, mv);
 		le = cudaGetLastError();
 	}
 	if (le != cudaSuccess && getenv("KLLM_GPU_DEBUG"))
@@ -775,16 +901,18 @@ extern "C" int kllm_prefill_launch(const struct kllm_prefill_args *a, void *stre
 {
 	if (a->head_dim != kD)
 		return (int)cudaErrorInvalidValue;
-	CUtensorMap mk, mv;
+	const int g = a->num_heads / a->num_kv_heads;
+	CUtensorMap mq, mk, mv;
 	if (!make_map(&mk, a->k, a->num_tokens, a->num_kv_heads) ||
-	    !make_map(&mv, a->v, a->num_tokens, a->num_kv_heads))
+	    !make_map(&mv, a->v, a->num_tokens, a->num_kv_heads) ||
+	    !make_q_map(&mq, a->q, a->num_tokens, a->num_heads, g))
 		return (int)cudaErrorInvalidValue;
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
-	switch (a->num_heads / a->num_kv_heads) {
-	case 1: return launch_g<1>(*a, mk, mv, st);
-	case 2: return launch_g<2>(*a, mk, mv, st);
-	case 4: return launch_g<4>(*a, mk, mv, st);
-	case 8: return launch_g<8>(*a, mk, mv, st);
+	switch (g) {
+	case 1: return launch_g<1>(*a, mq, mk, mv, st);
+	case 2: return launch_g<2>(*a, mq, mk, mv, st);
+	case 4: return launch_g<4>(*a, mq, mk, mv, st);
+	case 8: return launch_g<8>(*a, mq, mk, mv, st);
 	default: return (int)cudaErrorInvalidValue;
 	}
 }

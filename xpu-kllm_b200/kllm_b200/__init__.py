@@ -125,7 +125,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    p = path or LIB_PATH
+    p = path or os.environ.get("KLLM_GPU_LIB") or LIB_PATH
     if not os.path.exists(p):
         raise RuntimeError(f"libkllm_gpu.so not built: {p} (run __graft_entry__.build())")
     lib = ctypes.CDLL(p)
