@@ -34,7 +34,20 @@ def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False):
+def _random_bits_bf16(shape, seed):
+    """bf16 values with random signs and mantissas over 2^-20 .. 2^18 (38
+    binades, so every E4M3 scale code and many exact-midpoint quotients occur),
+    one in 16 zero."""
+    rng = np.random.default_rng(seed)
+    exp = rng.integers(107, 145, size=shape, dtype=np.uint16)
+    bits = (rng.integers(0, 2, size=shape, dtype=np.uint16) << 15) | (exp << 7) | \
+        rng.integers(0, 128, size=shape, dtype=np.uint16)
+    bits[rng.integers(0, 16, size=shape) == 0] = 0
+    return bits.astype(np.uint16)
+
+
+def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False,
+                 random_bits=False):
     """Random tokens appended at scattered positions of a few sequences."""
     cfg = replace(wl.C1, kv_dtype=kv if kv != 2 else wl.KV_BF16, block=block, d=d, hkv=hkv,
                   hq=hkv, arena_slots=None)
@@ -47,6 +60,9 @@ def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False):
     n = len(pos)
     k = wl.normal_bf16(seed, wl.ST_PK, 0, (n, hkv, d))
     v = wl.normal_bf16(seed, wl.ST_PV, 0, (n, hkv, d))
+    if random_bits:
+        k = _random_bits_bf16((n, hkv, d), seed)
+        v = _random_bits_bf16((n, hkv, d), seed + 1)
     if extreme:  # zeros, huge, tiny, subnormal-producing blocks, signed zeros
         kf = wl.bf16_to_f32(k).copy()
         kf[0, 0, :8] = 0.0
@@ -69,9 +85,9 @@ def _section_bytes(kv, block, d):
 
 @pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8, 2])
 @pytest.mark.parametrize("extreme", [False, True])
-def test_append_bit_exact(be, kv, extreme):
+def test_append_bit_exact(be, kv, extreme, random_bits=False):
     import torch
-    cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme)
+    cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme, random_bits=random_bits)
     sec = _section_bytes(kv, cfg.block, cfg.d)
     page = cfg.hkv * sec
     slot_bytes = 2 * page
@@ -109,6 +125,14 @@ def test_append_bit_exact(be, kv, extreme):
     if not np.array_equal(got, arena_h):
         diff = np.argwhere(got != arena_h)
         raise AssertionError(f"{len(diff)} bytes differ; first {diff[:5].tolist()}")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_MX_FP8, 2])
+def test_append_random_bits_bit_exact(be, kv):
+    """Quantize-on-write of random bf16 bit patterns over 38 binades: the
+    GPU's reciprocal-and-residual quotient must round to the same E4M3 codes
+    as the oracle's exact division, ties included."""
+    test_append_bit_exact(be, kv, False, random_bits=True)
 
 
 def test_append_compat_matches_reference_function(be):

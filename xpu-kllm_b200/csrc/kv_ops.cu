@@ -69,9 +69,18 @@ __device__ __forceinline__ uint32_t mx_scale_code(float amax)
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// One 8-element micro-block b of kv head h of row i (K if kv == 0, else V),
-// written to position pos of sequence seq.
-__device__ __forceinline__ void append_block(const kllm_append_args &a, int i, int seq,
+// Micro-block b (8 elements) of kv head h of row i of K (kv == 0) or V.
+__device__ __forceinline__ uint4 append_load(const kllm_append_args &a, int i, int h, int kv,
+					     int b)
+{
+	return *reinterpret_cast<const uint4 *>(
+	    reinterpret_cast<const uint8_t *>(kv ? a.v : a.k) +
+	    (((size_t)i * a.num_kv_heads + h) * a.head_dim + (size_t)b * 8) * 2);
+}
+
+// Writes micro-block x (b of kv head h, K or V) to position pos of sequence
+// seq: bf16 copy, MX-FP8 quantization, or the reference's BF16-payload form.
+__device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x, int seq,
 					     int pos, int h, int kv, int b)
 {
 	const int blk = pos >= 0 ? pos / a.block_size : -1;
@@ -92,9 +101,6 @@ __device__ __forceinline__ void append_block(const kllm_append_args &a, int i, i
 	const int d = a.head_dim, bs = a.block_size;
 	uint8_t *sec = reinterpret_cast<uint8_t *>(base) + a.layer_off +
 		       (size_t)h * section_bytes(a.kv_dtype, bs, d);
-	const uint4 x = *reinterpret_cast<const uint4 *>(
-	    reinterpret_cast<const uint8_t *>(kv ? a.v : a.k) +
-	    (((size_t)i * a.num_kv_heads + h) * d + (size_t)b * 8) * 2);
 
 	if (a.kv_dtype == 0) {
 		*reinterpret_cast<uint4 *>(sec + ((size_t)slot * d + b * 8) * 2) = x;
@@ -111,12 +117,24 @@ __device__ __forceinline__ void append_block(const kllm_append_args &a, int i, i
 		const uint32_t code = mx_scale_code(amax);
 		uint32_t lo = 0u, hi = 0u;
 		if (code != 0u) {
+			// x / s through the correctly rounded reciprocal plus one residual
+			// step (Markstein): exact whenever the quotient is representable,
+			// within one fp32 ulp otherwise. A bf16 x over an E4M3 s is either
+			// such an exact quotient or at least 2^-9 (relative) away from every
+			// E4M3 rounding midpoint, so the E4M3 rounding below equals that of
+			// the correctly rounded quotient.
 			const float s = e4m3_value(code);
+			const float y = __frcp_rn(s);
+			float q[8];
+#pragma unroll
+			for (int k = 0; k < 8; ++k) {
+				const float q0 = f[k] * y;
+				q[k] = fmaf(fmaf(-s, q0, f[k]), y, q0);
+			}
 			uint32_t p[4];
 #pragma unroll
 			for (int k = 0; k < 4; ++k)
-				p[k] = cvt_e4m3x2(__fdiv_rn(f[2 * k], s),
-						  __fdiv_rn(f[2 * k + 1], s));
+				p[k] = cvt_e4m3x2(q[2 * k], q[2 * k + 1]);
 			lo = p[0] | (p[1] << 16);
 			hi = p[2] | (p[3] << 16);
 		}
@@ -145,49 +163,70 @@ __device__ __forceinline__ void append_block(const kllm_append_args &a, int i, i
 	sec[(size_t)bs * d * 2 + (size_t)slot * (d / 8) + b] = amax > 0.f ? 64 : 0;
 }
 
-// One thread = one 8-element micro-block of one (token, K|V, kv head) row.
-__global__ void append_kernel(const kllm_append_args a)
+// Grid x = groups of kTokensPerCta tokens, y = 256-thread slices of a
+// token's 2 x num_kv_heads x head_dim/8 micro-blocks (K first, then V); one
+// thread per micro-block and token. Every thread first issues the data loads
+// of all its tokens, then resolves their pages, so several independent loads
+// are in flight per thread and a warp reads 512 contiguous bytes per token.
+constexpr int kTokensPerCta = 4;
+
+__device__ __forceinline__ void append_tokens(const kllm_append_args &a, int i0,
+					      const int *seqs, const int *poss)
 {
-	const int nb = a.head_dim / 8;
-	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
-	if (t >= total)
+	const int nb = a.head_dim >> 3;
+	const int per_kv = a.num_kv_heads * nb;
+	const int u = blockIdx.y * blockDim.x + threadIdx.x;
+	if (u >= 2 * per_kv)
 		return;
-	const int b = (int)(t % nb);
-	const long long r = t / nb;
-	const int h = (int)(r % a.num_kv_heads);
-	const int kv = (int)((r / a.num_kv_heads) % 2);
-	const int i = (int)(r / (2LL * a.num_kv_heads));
-	append_block(a, i, a.token_seq[i], a.token_pos[i], h, kv, b);
+	const int kv = u >= per_kv ? 1 : 0;
+	const int rem = u - kv * per_kv;
+	const int h = rem / nb, b = rem - h * nb;
+	uint4 x[kTokensPerCta];
+#pragma unroll
+	for (int t = 0; t < kTokensPerCta; ++t)
+		if (i0 + t < a.num_tokens)
+			x[t] = append_load(a, i0 + t, h, kv, b);
+#pragma unroll
+	for (int t = 0; t < kTokensPerCta; ++t)
+		if (i0 + t < a.num_tokens)
+			append_store(a, x[t], seqs[t], poss[t], h, kv, b);
+}
+
+__global__ void __launch_bounds__(256) append_kernel(const kllm_append_args a)
+{
+	const int i0 = blockIdx.x * kTokensPerCta;
+	int seqs[kTokensPerCta], poss[kTokensPerCta];
+#pragma unroll
+	for (int t = 0; t < kTokensPerCta; ++t) {
+		const bool in = i0 + t < a.num_tokens;
+		seqs[t] = in ? a.token_seq[i0 + t] : -1;
+		poss[t] = in ? a.token_pos[i0 + t] : -1;
+	}
+	append_tokens(a, i0, seqs, poss);
 }
 
 // Same, with the (sequence, position) of row i derived from chunk offsets.
-__global__ void append_chunk_kernel(const kllm_append_args a, const int *cu, const int *ctx)
+__global__ void __launch_bounds__(256) append_chunk_kernel(const kllm_append_args a,
+							   const int *cu, const int *ctx)
 {
-	const int nb = a.head_dim / 8;
-	const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-	const long long total = (long long)a.num_tokens * 2 * a.num_kv_heads * nb;
-	if (t >= total)
-		return;
-	const int b = (int)(t % nb);
-	const long long r = t / nb;
-	const int h = (int)(r % a.num_kv_heads);
-	const int kv = (int)((r / a.num_kv_heads) % 2);
-	const int i = (int)(r / (2LL * a.num_kv_heads));
-	int lo = 0, hi = a.num_seqs - 1;   // last s with cu[s] <= i
-	while (lo < hi) {
-		const int mid = (lo + hi + 1) >> 1;
-		if (cu[mid] <= i)
-			lo = mid;
-		else
-			hi = mid - 1;
+	__shared__ int s_seq[kTokensPerCta], s_pos[kTokensPerCta];
+	const int i0 = blockIdx.x * kTokensPerCta;
+	if (threadIdx.x < kTokensPerCta) {
+		const int i = i0 + threadIdx.x;
+		int lo = 0, hi = a.num_seqs - 1;   // last s with cu[s] <= i
+		while (lo < hi) {
+			const int mid = (lo + hi + 1) >> 1;
+			if (cu[mid] <= i)
+				lo = mid;
+			else
+				hi = mid - 1;
+		}
+		const bool in = i < a.num_tokens && i < cu[lo + 1];
+		s_seq[threadIdx.x] = in ? lo : -1;   // beyond the last chunk: flagged
+		s_pos[threadIdx.x] = in ? ctx[lo] + (i - cu[lo]) : -1;
 	}
-	if (i >= cu[lo + 1]) {             // i beyond the last chunk
-		if (a.err && b == 0)
-			atomicOr(a.err, 0x4u);
-		return;
-	}
-	append_block(a, i, lo, ctx[lo] + (i - cu[lo]), h, kv, b);
+	__syncthreads();
+	append_tokens(a, i0, s_seq, s_pos);
 }
 
 // One warp per (seq, kv head): walk the pages in order, skip invalid
@@ -291,14 +330,18 @@ __global__ void merge_kernel(const float *m, const float *l, const float *o,
 
 using namespace kllm;
 
+static dim3 append_grid(const struct kllm_append_args *a, int threads)
+{
+	const int per_token = 2 * a->num_kv_heads * (a->head_dim / 8);
+	return dim3((unsigned)((a->num_tokens + kTokensPerCta - 1) / kTokensPerCta),
+		    (unsigned)((per_token + threads - 1) / threads));
+}
+
 extern "C" int kllm_append_launch(const struct kllm_append_args *a, void *stream)
 {
-	const long long total = (long long)a->num_tokens * 2 * a->num_kv_heads * (a->head_dim / 8);
-	if (total <= 0)
+	if (a->num_tokens <= 0)
 		return 0;
-	const int threads = 256;
-	const long long blocks = (total + threads - 1) / threads;
-	append_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+	append_kernel<<<append_grid(a, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
 	return (int)cudaGetLastError();
 }
 
@@ -306,12 +349,9 @@ extern "C" int kllm_append_chunk_launch(const struct kllm_append_args *a,
 					const int *cu_seqlens, const int *ctx_lens,
 					void *stream)
 {
-	const long long total = (long long)a->num_tokens * 2 * a->num_kv_heads * (a->head_dim / 8);
-	if (total <= 0)
+	if (a->num_tokens <= 0)
 		return 0;
-	const int threads = 256;
-	const long long blocks = (total + threads - 1) / threads;
-	append_chunk_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+	append_chunk_kernel<<<append_grid(a, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
 	    *a, cu_seqlens, ctx_lens);
 	return (int)cudaGetLastError();
 }
