@@ -46,19 +46,19 @@ constexpr int kD = 128;             // head_dim
 constexpr int kHalf = 64;           // bf16 elements per 128-byte swizzle row
 constexpr int kTileBytes = kRows * kD * 2;    // 32 KB: one [128 x 128] bf16 tile
 constexpr int kHalfBytes = kTileBytes / 2;    // 16 KB: one 64-column half
-// A row's reference max is raised only when a score exceeds it by more than
-// 2^kSlackLog2, so P <= 2^30 (x 2^8 on cached MX blocks): finite in bf16 and
-// in the fp32 accumulators, and the raise (a rescale of O, l and the P
-// already written) is rare after a row's first keys.
-constexpr float kSlackLog2 = 30.f;
+// With the row's block max known before P is written, the reference is
+// raised whenever a block max exceeds it by 2^8 (P <= 256, x 2^8 on cached
+// MX blocks); that costs one O rescale.
+constexpr float kRaiseLog2 = 8.f;
 #ifndef KLLM_PF_WAIT_HINT
 #define KLLM_PF_WAIT_HINT 20000   // try_wait suspend hint, ns (0: plain try_wait)
 #endif
 constexpr uint64_t kWaitNs = 200000000ull;  // 200 ms: a healthy wait takes microseconds
 
 constexpr int kStages = 2;
-constexpr int kWarpsSoftmax = 8, kWarpProducer0 = 8, kWarpMma = 12;
-constexpr int kThreads = 13 * 32;
+constexpr int kWarpsSoftmax = 8, kWarpMma = 8, kWarpProducer0 = 9;
+constexpr int kProducerThreads = 96;
+constexpr int kThreads = 12 * 32;
 
 struct PrefillSmem {
 	// tiles: two 64-column halves of 128 rows x 128 B, SW128
@@ -153,28 +153,6 @@ __device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const float (&v
 		        "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]),
 		        "f"(v[13]), "f"(v[14]), "f"(v[15])
 		     : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_ld4(uint32_t (&a)[16], uint32_t (&b)[16],
-					      uint32_t (&c)[16], uint32_t (&d)[16])
-{
-	// one wait for four prefetched loads; every register is an in/out operand
-	asm volatile("tcgen05.wait::ld.sync.aligned;"
-		     : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
-		       "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
-		       "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
-		       "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]),
-		       "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
-		       "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
-		     :: "memory");
-	asm volatile("tcgen05.wait::ld.sync.aligned;"
-		     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]), "+r"(c[4]), "+r"(c[5]),
-		       "+r"(c[6]), "+r"(c[7]), "+r"(c[8]), "+r"(c[9]), "+r"(c[10]), "+r"(c[11]),
-		       "+r"(c[12]), "+r"(c[13]), "+r"(c[14]), "+r"(c[15]),
-		       "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3]), "+r"(d[4]), "+r"(d[5]),
-		       "+r"(d[6]), "+r"(d[7]), "+r"(d[8]), "+r"(d[9]), "+r"(d[10]), "+r"(d[11]),
-		       "+r"(d[12]), "+r"(d[13]), "+r"(d[14]), "+r"(d[15])
-		     :: "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -407,76 +385,91 @@ __device__ __forceinline__ void rescale_row(uint32_t tS, uint32_t tO, float f, b
 	}
 }
 
-template <bool FULL>
-__device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const uint32_t (&vmask)[4],
-					      float sl2, float pexp, bool o_live, float &m_ref,
-					      float &l_sum)
+// Waits for this thread's outstanding TMEM loads; all 128 destination
+// registers are in/out operands, so their uses follow the wait.
+__device__ __forceinline__ void tmem_wait_ld_row(uint32_t (&r)[8][16])
 {
+#pragma unroll
+	for (int q = 0; q < 4; ++q)
+		asm volatile("tcgen05.wait::ld.sync.aligned;"
+			     : "+r"(r[2 * q][0]), "+r"(r[2 * q][1]), "+r"(r[2 * q][2]), "+r"(r[2 * q][3]),
+			       "+r"(r[2 * q][4]), "+r"(r[2 * q][5]), "+r"(r[2 * q][6]), "+r"(r[2 * q][7]),
+			       "+r"(r[2 * q][8]), "+r"(r[2 * q][9]), "+r"(r[2 * q][10]), "+r"(r[2 * q][11]),
+			       "+r"(r[2 * q][12]), "+r"(r[2 * q][13]), "+r"(r[2 * q][14]), "+r"(r[2 * q][15]),
+			       "+r"(r[2 * q + 1][0]), "+r"(r[2 * q + 1][1]), "+r"(r[2 * q + 1][2]),
+			       "+r"(r[2 * q + 1][3]), "+r"(r[2 * q + 1][4]), "+r"(r[2 * q + 1][5]),
+			       "+r"(r[2 * q + 1][6]), "+r"(r[2 * q + 1][7]), "+r"(r[2 * q + 1][8]),
+			       "+r"(r[2 * q + 1][9]), "+r"(r[2 * q + 1][10]), "+r"(r[2 * q + 1][11]),
+			       "+r"(r[2 * q + 1][12]), "+r"(r[2 * q + 1][13]), "+r"(r[2 * q + 1][14]),
+			       "+r"(r[2 * q + 1][15])
+			     :: "memory");
+}
+
+// One 128-key block of one row, held in registers: S (TMEM columns of tS)
+// -> P written back in place as 8 groups of (8 hi, 8 lo) bf16 pairs,
+// p = 2^pexp x exp2(s x sl2 - m_ref); l_sum gains sum(p) / 2^pexp. Invalid
+// keys are set to -inf first (p = 0). The row's block max is known before
+// any P is written, so raising the reference max rescales only O and l.
+// o_live: O already holds earlier blocks. Branches around TMEM accesses are
+// warp-uniform.
+__device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const uint32_t (&vmask)[4],
+					      bool masked, float sl2, float pexp, bool o_live,
+					      float &m_ref, float &l_sum)
+{
+	uint32_t r[8][16];
+#pragma unroll
+	for (int g = 0; g < 8; ++g)
+		tmem_ld16_nowait(tS + 16 * g, r[g]);
+	tmem_wait_ld_row(r);
+	if (masked) {
+#pragma unroll
+		for (int k = 0; k < 128; ++k)
+			if (!((vmask[k >> 5] >> (k & 31)) & 1u))
+				r[k >> 4][k & 15] = 0xFF800000u;   // -inf
+	}
+	float mv[8];                           // 8 independent chains of 16, then a tree
+#pragma unroll
+	for (int i = 0; i < 8; ++i)
+		mv[i] = __uint_as_float(r[0][i]);
+#pragma unroll
+	for (int k = 8; k < 128; ++k)
+		mv[k & 7] = fmaxf(mv[k & 7], __uint_as_float(r[k >> 4][k & 15]));
+#pragma unroll
+	for (int w = 4; w >= 1; w >>= 1)      // tree max
+#pragma unroll
+		for (int i = 0; i < w; ++i)
+			mv[i] = fmaxf(mv[i], mv[i + w]);
+	const float gl = mv[0] * sl2;
+	const bool raise = gl > m_ref + kRaiseLog2;
+	if (__any_sync(0xffffffffu, raise)) {
+		const float f = raise ? exp2f(m_ref - gl) : 1.f;
+		if (o_live)
+			rescale_row(tS, tO, f, true, 0);
+		l_sum *= f;
+		if (raise)
+			m_ref = gl;
+	}
+	// no valid key yet (m_ref = -inf): every p is 0, not exp2(-inf + inf)
+	const float moff = m_ref == -CUDART_INF_F ? -CUDART_INF_F : pexp - m_ref;
 	float bsum = 0.f;
-	// two halves of 64 keys: four 16-column loads in flight, one max tree and
-	// one warp vote per half
 #pragma unroll
-	for (int hb = 0; hb < 2; ++hb) {
-		uint32_t r0[16], r1[16], r2[16], r3[16];
-		tmem_ld16_nowait(tS + 64 * hb, r0);
-		tmem_ld16_nowait(tS + 64 * hb + 16, r1);
-		tmem_ld16_nowait(tS + 64 * hb + 32, r2);
-		tmem_ld16_nowait(tS + 64 * hb + 48, r3);
-		tmem_wait_ld4(r0, r1, r2, r3);
-		float v[64];
+	for (int g = 0; g < 8; ++g) {
+		float w[16];
 #pragma unroll
-		for (int i = 0; i < 16; ++i) {
-			v[i] = __uint_as_float(r0[i]);
-			v[16 + i] = __uint_as_float(r1[i]);
-			v[32 + i] = __uint_as_float(r2[i]);
-			v[48 + i] = __uint_as_float(r3[i]);
+		for (int i = 0; i < 8; ++i) {
+			const float q0 = ex2_approx(fmaf(__uint_as_float(r[g][2 * i]), sl2, moff));
+			const float q1 = ex2_approx(fmaf(__uint_as_float(r[g][2 * i + 1]), sl2, moff));
+			bsum += q0 + q1;
+			pack_p_pair(q0, q1, w[i], w[8 + i]);
 		}
-		const uint32_t m0 = FULL ? 0xFFFFFFFFu : vmask[2 * hb], m1 = FULL ? 0xFFFFFFFFu : vmask[2 * hb + 1];
-		auto valid = [&](int i) -> bool {
-			return FULL || (((i < 32 ? m0 : m1) >> (i & 31)) & 1u);
-		};
-		float mv[32];
-#pragma unroll
-		for (int i = 0; i < 32; ++i)
-			mv[i] = fmaxf(valid(i) ? v[i] : -CUDART_INF_F, valid(32 + i) ? v[32 + i] : -CUDART_INF_F);
-#pragma unroll
-		for (int w = 16; w >= 1; w >>= 1)     // tree max
-#pragma unroll
-			for (int i = 0; i < w; ++i)
-				mv[i] = fmaxf(mv[i], mv[i + w]);
-		const float gl = mv[0] * sl2;
-		const bool raise = gl > m_ref + kSlackLog2;
-		if (__any_sync(0xffffffffu, raise)) {
-			// rare: move the reference up, rescale what was built on the old one
-			const float f = raise ? exp2f(m_ref - gl) : 1.f;
-			rescale_row(tS, tO, f, o_live, 4 * hb);
-			bsum *= f;
-			l_sum *= f;
-			if (raise)
-				m_ref = gl;
-		}
-		const float moff = pexp - m_ref;
-		// 16-key group g of this half -> 8 hi pairs, then 8 lo pairs
-#pragma unroll
-		for (int g = 0; g < 4; ++g) {
-			float w[16];
-#pragma unroll
-			for (int i = 0; i < 8; ++i) {
-				const int k0 = 16 * g + 2 * i;
-				const float q0 = valid(k0) ? ex2_approx(fmaf(v[k0], sl2, moff)) : 0.f;
-				const float q1 = valid(k0 + 1) ? ex2_approx(fmaf(v[k0 + 1], sl2, moff)) : 0.f;
-				bsum += q0 + q1;
-				pack_p_pair(q0, q1, w[i], w[8 + i]);
-			}
-			tmem_st16_nowait(tS + 64 * hb + 16 * g, w);
-		}
+		tmem_st16_nowait(tS + 16 * g, w);
 	}
 	tmem_wait_st();
 	l_sum += bsum * exp2f(-pexp);
 }
 
 template <int G>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__(168)
 prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm_q,
 	       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v)
 {
@@ -582,10 +575,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			const float pexp = prior && a.kv_dtype == 1 ? 8.f : 0.f;
 			const bool full = __all_sync(0xffffffffu, (vmask[0] & vmask[1] & vmask[2] &
 								   vmask[3]) == 0xFFFFFFFFu);
-			if (full)
-				softmax_block<true>(tS, tO, vmask, sl2, pexp, j > 0, m_ref, l_sum);
-			else
-				softmax_block<false>(tS, tO, vmask, sl2, pexp, j > 0, m_ref, l_sum);
+			softmax_block(tS, tO, vmask, !full, sl2, pexp, j > 0, m_ref, l_sum);
 			tc_fence_before();
 			mbar_arrive(&sm.p_full[t]);
 		}
@@ -613,9 +603,9 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					    pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
 			}
 		}
-	} else if (warp < kWarpMma) {
+	} else if (warp >= kWarpProducer0) {
 		// ================= producer ==============================================
-		const int pt = tid - kWarpProducer0 * 32;          // 0..127: one row each
+		const int pt = tid - kWarpProducer0 * 32;          // 0..95
 		if (pt == 0) {
 			// both query tiles by TMA: box {64 dims, G heads, BQ tokens} per half
 			mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
@@ -637,11 +627,13 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					okw = fill == 0 || wait_or_abort(sm, &sm.v_empty[st], par, a);
 				sm.prod_ok[j & 1] = okw;
 			}
-			asm volatile("bar.sync 1, 128;" ::: "memory");
+			asm volatile("bar.sync 1, 96;" ::: "memory");
 			if (!*reinterpret_cast<volatile int *>(&sm.prod_ok[j & 1]))
 				break;
 			if (prior) {
-				const int kpos = j * kKeys + pt;
+#pragma unroll 1
+			for (int row = pt; row < kKeys; row += kProducerThreads) {   // warp-uniform
+				const int kpos = j * kKeys + row;
 				int slot = 0;
 				const uint8_t *ks = nullptr, *vs = nullptr;
 				if (kpos < ctx_cap) {
@@ -677,7 +669,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 						uint32_t w[32];
 						mx_dequant_half(sm.lut, pay + 4 * half,
 								half ? make_uint2(sc.z, sc.w) : make_uint2(sc.x, sc.y), w);
-						store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+						store_half_row(part < 2 ? sm.k[st] : sm.v[st], row, half, w);
 					}
 				} else {
 #pragma unroll 1
@@ -691,14 +683,15 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 							for (int i = 0; i < 32; ++i)
 								w[i] = 0u;
 						}
-						store_half_row(part < 2 ? sm.k[st] : sm.v[st], pt, half, w);
+						store_half_row(part < 2 ? sm.k[st] : sm.v[st], row, half, w);
 					}
 				}
 				const uint32_t ball = __ballot_sync(0xffffffffu, okk);
 				if (lane == 0)
-					sm.key_ok[st][pt >> 5] = ball;
+					sm.key_ok[st][row >> 5] = ball;
+			}
 				fence_async_smem();
-				asm volatile("bar.sync 1, 128;" ::: "memory");
+				asm volatile("bar.sync 1, 96;" ::: "memory");
 				if (pt == 0) {
 					mbar_arrive(&sm.k_full[st]);
 					mbar_arrive(&sm.v_full[st]);
