@@ -129,6 +129,15 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar)
 		     :: "r"(smem_u32(bar)) : "memory");
 }
 
+// true in exactly one lane of the (fully active) warp
+__device__ __forceinline__ bool elect_one()
+{
+	uint32_t is;
+	asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+		     : "=r"(is));
+	return is != 0;
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -723,46 +732,73 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					mbar_wait_ns(&sm.v_full[st], (uint32_t)(issued_v[st] & 1), kWaitNs);
 			}
 		}
-	} else if (lane == 0) {
+	} else {
 		// ================= MMA issue =============================================
+		// The whole warp runs this role, so the descriptors and addresses are
+		// warp-uniform values; one elected lane issues the MMAs and commits.
+		const bool leader = elect_one();
 		const uint32_t id_s = umma_idesc(false), id_pv = umma_idesc(true);
 		const uint32_t sq[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
+		// Operand descriptors are built once: a k-step adds (byte offset >> 4)
+		// to the start-address field (bits 0-13), which cannot carry out since
+		// shared-memory addresses stay below 2^18. Issue is the single thread's
+		// critical path (it shares its scheduler with two softmax warps), so
+		// each MMA costs one 64-bit add here.
+		const uint64_t dq0 = umma_desc(sq[0], 16u, 1024u), dq1 = umma_desc(sq[1], 16u, 1024u);
+		const uint64_t dk0 = umma_desc(smem_u32(sm.k[0]), 16u, 1024u);
+		const uint64_t dk1 = umma_desc(smem_u32(sm.k[1]), 16u, 1024u);
+		const uint64_t dv0 = umma_desc(smem_u32(sm.v[0]), (uint32_t)kHalfBytes, 1024u);
+		const uint64_t dv1 = umma_desc(smem_u32(sm.v[1]), (uint32_t)kHalfBytes, 1024u);
+		static_assert(kStages == 2, "descriptor selection assumes two stages");
 		auto issue_s = [&](int t, int st) {
-			const uint32_t sk = smem_u32(sm.k[st]);
+			const uint64_t dq = t ? dq1 : dq0, dk = st ? dk1 : dk0;
+			const uint32_t d = tmem + col_s(t);
 #pragma unroll
 			for (int kk = 0; kk < kD / 16; ++kk) {
-				const uint32_t off = (uint32_t)(kk >> 2) * kHalfBytes + (uint32_t)(kk & 3) * 32u;
-				umma_f16(tmem + col_s(t), umma_desc(sq[t] + off, 16u, 1024u),
-					 umma_desc(sk + off, 16u, 1024u), id_s, kk > 0);
+				const uint64_t off = ((uint64_t)(kk >> 2) * kHalfBytes + (uint64_t)(kk & 3) * 32u) >> 4;
+				if (leader)
+					umma_f16(d, dq + off, dk + off, id_s, kk > 0);
 			}
+			__syncwarp();
 		};
 		auto issue_pv = [&](int t, int st, bool first) {
-			const uint32_t sv = smem_u32(sm.v[st]);
+			const uint64_t dv = st ? dv1 : dv0;
+			const uint32_t d = tmem + col_o(t), pa = tmem + col_s(t);
 #pragma unroll
 			for (int kk = 0; kk < 2 * kKeys / 16; ++kk) {
 				const int g = kk >> 1;     // 16-key group; kk odd: the lo half of P
-				umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + 16u * g + 8u * (kk & 1),
-					    umma_desc(sv + (uint32_t)g * 2048u, (uint32_t)kHalfBytes, 1024u),
-					    id_pv, (first && kk == 0) ? 0u : 1u);
+				if (leader)
+					umma_f16_ts(d, pa + 16u * g + 8u * (kk & 1), dv + (uint64_t)((g * 2048) >> 4),
+						    id_pv, (first && kk == 0) ? 0u : 1u);
 			}
+			__syncwarp();
 		};
-		bool ok = wait_or_abort(sm, &sm.q_full, 0u, a) &&
-			  wait_or_abort(sm, &sm.k_full[0], 0u, a);
+		auto commit = [&](uint64_t *bar) {
+			if (leader)
+				umma_commit(bar);
+			__syncwarp();
+		};
+		// every lane waits; the outcome is made warp-uniform
+		auto wait_all = [&](uint64_t *bar, uint32_t parity) {
+			return __all_sync(0xffffffffu, wait_or_abort(sm, bar, parity, a));
+		};
+		bool ok = wait_all(&sm.q_full, 0u);
+		ok = ok && wait_all(&sm.k_full[0], 0u);
 		if (ok) {
 			tc_fence_after();
 			for (int t = 0; t < 2; ++t)
 				if (nb_t[t] > 0) {
 					issue_s(t, 0);
-					umma_commit(&sm.s_full[t]);
+					commit(&sm.s_full[t]);
 				}
-			umma_commit(&sm.k_empty[0]);
+			commit(&sm.k_empty[0]);
 		}
 		for (int j = 0; j < nb && ok; ++j) {
 			const int st = j % kStages, ns = (j + 1) % kStages;
-			ok = wait_or_abort(sm, &sm.v_full[st], (uint32_t)((j / kStages) & 1), a);
+			ok = wait_all(&sm.v_full[st], (uint32_t)((j / kStages) & 1));
 			for (int t = 0; t < 2 && ok; ++t) {
 				if (j < nb_t[t]) {
-					if (!wait_or_abort(sm, &sm.p_full[t], (uint32_t)(j & 1), a)) {
+					if (!wait_all(&sm.p_full[t], (uint32_t)(j & 1))) {
 						ok = false;
 						break;
 					}
@@ -770,11 +806,10 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 					issue_pv(t, st, j == 0);
 				}
 				if (t == 1)
-					umma_commit(&sm.v_empty[st]);   // both PV(j) issued: V(j) free when done
+					commit(&sm.v_empty[st]);   // both PV(j) issued: V(j) free when done
 				if (t == 0 && j + 1 < nb) {
 					// K of block j + 1, for both tiles' next S
-					if (!wait_or_abort(sm, &sm.k_full[ns], (uint32_t)(((j + 1) / kStages) & 1),
-							   a)) {
+					if (!wait_all(&sm.k_full[ns], (uint32_t)(((j + 1) / kStages) & 1))) {
 						ok = false;
 						break;
 					}
@@ -782,16 +817,16 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 				}
 				if (j + 1 < nb_t[t]) {
 					issue_s(t, ns);
-					umma_commit(&sm.s_full[t]);
+					commit(&sm.s_full[t]);
 				} else if (j + 1 == nb_t[t]) {
-					umma_commit(&sm.o_full[t]);
+					commit(&sm.o_full[t]);
 				}
 			}
 			if (ok && j + 1 < nb)
-				umma_commit(&sm.k_empty[ns]);       // both S(j + 1) issued
+				commit(&sm.k_empty[ns]);       // both S(j + 1) issued
 		}
-		// drain: every MMA issued by this thread completes before TMEM is freed
-		umma_commit(&sm.drain);
+		// drain: every MMA issued by the leader completes before TMEM is freed
+		commit(&sm.drain);
 		mbar_wait_ns(&sm.drain, 0u, kWaitNs);
 	}
 
