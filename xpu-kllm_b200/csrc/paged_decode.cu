@@ -918,14 +918,18 @@ decode_kernel(const kllm_decode_args a)
 }
 
 // Wide merge of the queued long segments: one CTA of 8 warps per
-// (segment, query head); warp w folds pieces w, w+8, ... with the
-// log-sum-exp rule, the warps are combined in shared memory. The last CTA
-// to finish clears the list header for the next launch.
+// (segment, query head). Pass 1: the segment's maximum over all its pieces
+// (independent loads by all threads, block reduction). Pass 2: warp w sums
+// pieces w, w+8, ... (o and l, each piece relative to its own maximum m,
+// weighted by exp2(m - maximum)) four pieces in flight, so
+// the loads do not wait on one another; the warps' sums are added in shared
+// memory. The last CTA to finish clears the list header for the next launch.
 template <int D>
 __global__ void __launch_bounds__(256)
 merge_big_kernel(const kllm_decode_args a, float unbias)
 {
-	__shared__ float sm_m[8], sm_l[8];
+	__shared__ float sm_red[8];
+	__shared__ float sm_l[8];
 	__shared__ float sm_o[8][D];
 	__shared__ int last;
 	ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
@@ -942,48 +946,79 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 		const int hh = (int)(pr % a.group);
 		const long long w0 = owner_warp(it.seg_x0, T, W);
 		const long long np = owner_warp(it.seg_x0 + it.ts - 1, T, W) - w0 + 1;
-		float M = -CUDART_INF_F, L = 0.f, acc[NV];
+		auto slot_of = [&](long long r) -> const float * {
+			const long long wr = w0 + r;
+			const int which = (r == 0 && wr * T / W != it.seg_x0) ? 1 : 0;
+			return a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
+		};
+		// ---- pass 1: segment maximum (log2 domain) over pieces with mass -----
+		float mx = -CUDART_INF_F;
+		for (long long r = threadIdx.x; r < np; r += blockDim.x) {
+			const float *sl = slot_of(r);
+			const float lr = __ldcg(sl + kSlotL + hh), mr = __ldcg(sl + kSlotM + hh);
+			if (lr > 0.f)
+				mx = fmaxf(mx, mr);
+		}
+#pragma unroll
+		for (int off = 16; off > 0; off >>= 1)
+			mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+		if (lane == 0)
+			sm_red[warp] = mx;
+		__syncthreads();
+		float Mt = sm_red[0];
+#pragma unroll
+		for (int w = 1; w < 8; ++w)
+			Mt = fmaxf(Mt, sm_red[w]);
+		// ---- pass 2: weighted sums against Mt, 4 pieces in flight per warp -----
+		float L = 0.f, acc[NV];
 #pragma unroll
 		for (int i = 0; i < NV; ++i)
 			acc[i] = 0.f;
-		for (long long r = warp; r < np; r += 8) {
-			const long long wr = w0 + r;
-			const int which = (r == 0 && wr * T / W != it.seg_x0) ? 1 : 0;
-			const float *slot = a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
-			const float lr = __ldcg(slot + kSlotL + hh);
-			if (!(lr > 0.f))
-				continue;
-			const float mr = __ldcg(slot + kSlotM + hh);
-			const float mn = fmaxf(M, mr);
-			const float fo = exp2f(M - mn), fr = exp2f(mr - mn);
-			L = L * fo + lr * fr;
-			M = mn;
-			const float *src = slot + kSlotO + hh * D + lane * NV;
+		for (long long r0 = warp; r0 < np; r0 += 32) {
+			float lr[4], mr[4], ov[4][NV];
 #pragma unroll
-			for (int i = 0; i < NV; ++i)
-				acc[i] = acc[i] * fo + __ldcg(src + i) * fr;
+			for (int u = 0; u < 4; ++u) {
+				const long long r = r0 + 8 * u;
+				lr[u] = 0.f;
+				mr[u] = 0.f;
+#pragma unroll
+				for (int i = 0; i < NV; ++i)
+					ov[u][i] = 0.f;
+				if (r < np) {
+					const float *sl = slot_of(r);
+					lr[u] = __ldcg(sl + kSlotL + hh);
+					mr[u] = __ldcg(sl + kSlotM + hh);
+					const float *src = sl + kSlotO + hh * D + lane * NV;
+#pragma unroll
+					for (int i = 0; i < NV; ++i)
+						ov[u][i] = __ldcg(src + i);
+				}
+			}
+#pragma unroll
+			for (int u = 0; u < 4; ++u) {
+				// a piece's o is unnormalised (relative to its own max m): it
+				// weighs exp2(m - Mt); its l weighs the same into L
+				const float e = lr[u] > 0.f ? exp2f(mr[u] - Mt) : 0.f;
+				L = fmaf(lr[u], e, L);
+#pragma unroll
+				for (int i = 0; i < NV; ++i)
+					acc[i] = fmaf(ov[u][i], e, acc[i]);
+			}
 		}
-		if (lane == 0) {
-			sm_m[warp] = M;
+		if (lane == 0)
 			sm_l[warp] = L;
-		}
 #pragma unroll
 		for (int i = 0; i < NV; ++i)
 			sm_o[warp][lane * NV + i] = acc[i];
 		__syncthreads();
 		if (threadIdx.x < D) {
 			const int d = threadIdx.x;
-			float Mt = -CUDART_INF_F;
-			for (int w = 0; w < 8; ++w)
-				if (sm_l[w] > 0.f)
-					Mt = fmaxf(Mt, sm_m[w]);
 			float Lt = 0.f, o = 0.f;
-			for (int w = 0; w < 8; ++w)
-				if (sm_l[w] > 0.f) {
-					const float f = exp2f(sm_m[w] - Mt);
-					Lt += sm_l[w] * f;
-					o += sm_o[w][d] * f;
-				}
+#pragma unroll
+			for (int w = 0; w < 8; ++w) {
+				Lt += sm_l[w];
+				o += sm_o[w][d];
+			}
 			const size_t row = (size_t)it.s * a.num_heads + (size_t)it.h * a.group + hh;
 			const float inv = Lt > 0.f ? unbias / Lt : 0.f;
 			if (a.pm) {
