@@ -1,0 +1,37 @@
+# SPDX-License-Identifier: Apache-2.0
+"""bench.py's reference arm (CPU only) prints one JSON line with the keys
+the benchmark contract names."""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def _run(*args) -> dict:
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args],
+                         capture_output=True, text=True, timeout=600, cwd=ROOT, check=True)
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_json_line():
+    line = _run("--impl", "reference", "--config", "c2_mxfp8_b64_ctx512-4096", "--steps", "1",
+                "--warmup", "3", "--cpu-seconds", "0.5")
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference"
+    assert line["config"]["workload"] == "c2_mxfp8_b64_ctx512-4096"
+    assert line["value"] > 0 and line["unit"] == "GB/s"
+    cb = line["cpu_baseline"]
+    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert line["warmup"] >= 3
