@@ -175,22 +175,39 @@ class DecodeRig:
 
     split_kv = False
 
-    def enable_split_kv(self, rank: int, world: int, dist) -> None:
-        """Cross-GPU split-KV: partial triples per rank, merged over NCCL by
-        the library (kllm_gpu_comm_merge) inside every step."""
+    def enable_split_kv(self, rank: int, world: int, dist, merge: str = "p2p") -> None:
+        """Cross-GPU split-KV: partial triples per rank, exchanged and merged
+        inside every step, either by one peer-memory kernel per rank
+        (kllm_gpu_p2p_merge) or over NCCL (kllm_gpu_comm_merge)."""
         import ctypes
         torch, c = self.torch, self.cfg
-        uid = (ctypes.c_uint8 * 128)()
-        if rank == 0:
-            rc = self.be.lib.kllm_gpu_comm_get_unique_id(uid)
-            assert rc == 0, f"comm id: {rc}"
-        t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
-        dist.broadcast(t, 0)
-        uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
-        rc = self.be.lib.kllm_gpu_comm_init(self.be.ctx, world, rank, uid, 120000)
-        if rc != 0:
-            raise RuntimeError(f"kllm_gpu_comm_init: {rc}")
         rows = self.B * c.hq
+        self.merge = merge
+        if merge == "p2p":
+            h = (ctypes.c_uint8 * 64)()
+            rc = self.be.lib.kllm_gpu_p2p_export(self.be.ctx, rows, c.d, h)
+            if rc != 0:
+                raise RuntimeError(f"kllm_gpu_p2p_export: {rc}")
+            mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device="cuda")
+            allh = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allh, mine)
+            blob = bytes(torch.cat(allh).cpu().tolist())
+            rc = self.be.lib.kllm_gpu_p2p_import(self.be.ctx, world, rank,
+                                                 (ctypes.c_uint8 * len(blob))(*blob))
+            if rc != 0:
+                raise RuntimeError(f"kllm_gpu_p2p_import: {rc}")
+            self.p2p_err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        else:
+            uid = (ctypes.c_uint8 * 128)()
+            if rank == 0:
+                rc = self.be.lib.kllm_gpu_comm_get_unique_id(uid)
+                assert rc == 0, f"comm id: {rc}"
+            t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
+            dist.broadcast(t, 0)
+            uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
+            rc = self.be.lib.kllm_gpu_comm_init(self.be.ctx, world, rank, uid, 120000)
+            if rc != 0:
+                raise RuntimeError(f"kllm_gpu_comm_init: {rc}")
         self.pm = torch.empty((rows,), dtype=torch.float32, device="cuda")
         self.pl = torch.empty_like(self.pm)
         self.po = torch.empty((rows, c.d), dtype=torch.float32, device="cuda")
@@ -211,7 +228,14 @@ class DecodeRig:
         rc = self.be.decode_v2(**kw)
         if rc != 0:
             raise RuntimeError(f"decode launch failed: {rc}")
-        if self.split_kv:
+        if self.split_kv and self.merge == "p2p":
+            rc = self.be.lib.kllm_gpu_p2p_merge(
+                self.be.ctx, self.pm.data_ptr(), self.pl.data_ptr(), self.po.data_ptr(),
+                self.B * c.hq, c.d, out_ptr or self.out[layer].data_ptr(),
+                self.p2p_err.data_ptr(), 2000, stream)
+            if rc != 0:
+                raise RuntimeError(f"kllm_gpu_p2p_merge failed: {rc}")
+        elif self.split_kv:
             rc = self.be.lib.kllm_gpu_comm_merge(
                 self.be.ctx, self.pm.data_ptr(), self.pl.data_ptr(), self.po.data_ptr(),
                 self.B * c.hq, c.d, out_ptr or self.out[layer].data_ptr(), stream, 0)
@@ -291,7 +315,7 @@ def run_kllm(args) -> None:
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     if split_kv:
-        rig.enable_split_kv(rank, world, dist)
+        rig.enable_split_kv(rank, world, dist, args.merge)
 
     def barrier():
         if world > 1:
@@ -320,6 +344,8 @@ def run_kllm(args) -> None:
     clocks = clk.stop()
     launches = be.stats().launches - launches0
     elapsed_ms = t0.elapsed_time(t1)
+    if rig.split_kv and rig.merge == "p2p" and int(rig.p2p_err.item()) != 0:
+        raise RuntimeError(f"peer-memory exchange error word {int(rig.p2p_err.item()):#x}")
     # mean decode launch = the timed region / decode launches: only the decode
     # (and its merge, which is empty unless a segment has > 16 pieces) runs
     # there; an event pair around every launch would cost 1-4% by itself
@@ -398,8 +424,11 @@ def run_kllm(args) -> None:
                        "arena_gb_rank0": round(float(allst[0, 5]) / 1e9, 2),
                        "arena_layout": args.arena_layout,
                        "l2": "inputs larger than L2 (KV per step >> 126 MB)",
-                       "parallelism": (f"split-KV x{world} (page ranges) + NCCL all-gather "
-                                       f"merge" if split_kv else
+                       "parallelism": ((f"split-KV x{world} (page ranges) + one peer-memory "
+                                        f"exchange-and-merge kernel per rank (NVLink)"
+                                        if args.merge == "p2p" else
+                                        f"split-KV x{world} (page ranges) + NCCL all-gather "
+                                        f"merge") if split_kv else
                                        f"request-sharded x{world} (LPT), no collective")},
             "tokens_per_s": round(total_tokens * args.steps / (t_ms * 1e-3), 1),
             "hbm_frac_8tbs": round(value / world / 8000.0, 4),
@@ -820,6 +849,9 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--merge", default="p2p", choices=["p2p", "nccl"],
+                    help="split-KV exchange at N > 1 (one long context): peer-memory kernel "
+                         "or NCCL all-gather + merge kernel")
     ap.add_argument("--arena-layout", default="layer-major",
                     choices=["layer-major", "slot-major"],
                     help="layer-major: each layer's pages form one region (layer_stride = "

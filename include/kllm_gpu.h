@@ -377,6 +377,30 @@ int kllm_gpu_comm_merge(struct kllm_gpu_ctx *ctx, const float *m,
 			int head_dim, void *out, void *stream, int timeout_ms);
 void kllm_gpu_comm_destroy(struct kllm_gpu_ctx *ctx);
 
+/* Cross-GPU split-KV exchange over peer memory (no counterpart in the
+ * reference): the same result as kllm_gpu_comm_merge, computed by one kernel
+ * per rank that stores this rank's triples into every peer's exchange
+ * buffer over NVLink (CUDA IPC mappings, plain stores), raises per-block
+ * flags there, waits (bounded) for the peers' flags and merges. One process
+ * per GPU on one node.
+ *   1. kllm_gpu_p2p_export on every rank: allocates the exchange buffer for
+ *      up to max_rows rows (<= 65536) of head_dim (64 or 128) and returns its
+ *      KLLM_P2P_HANDLE_BYTES-byte IPC handle;
+ *   2. the handles reach every rank through the caller's channel;
+ *   3. kllm_gpu_p2p_import with all ranks' handles (rank-major, nranks <= 8);
+ *   4. kllm_gpu_p2p_merge on every rank, in the same order on all ranks (each
+ *      call is one exchange epoch). A wait that expires ORs KLLM_ERR_TIMEOUT
+ *      into *err_word (optional) instead of hanging. */
+#define KLLM_P2P_HANDLE_BYTES 64
+int kllm_gpu_p2p_export(struct kllm_gpu_ctx *ctx, int max_rows, int head_dim,
+			uint8_t handle[KLLM_P2P_HANDLE_BYTES]);
+int kllm_gpu_p2p_import(struct kllm_gpu_ctx *ctx, int nranks, int rank,
+			const uint8_t *handles);
+int kllm_gpu_p2p_merge(struct kllm_gpu_ctx *ctx, const float *m, const float *l,
+		       const float *o, int num_rows, int head_dim, void *out,
+		       uint32_t *err_word, int timeout_ms, void *stream);
+void kllm_gpu_p2p_destroy(struct kllm_gpu_ctx *ctx);
+
 #ifdef __cplusplus
 }
 #endif

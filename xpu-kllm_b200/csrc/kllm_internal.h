@@ -116,6 +116,23 @@ int kllm_merge_launch(const float *m, const float *l, const float *o,
 		      int num_parts, int num_rows, int head_dim, void *out,
 		      void *stream);
 
+/* Peer-memory split-KV exchange + merge (p2p_merge.cu). */
+#define KLLM_P2P_MAX_RANKS 8
+#define KLLM_P2P_MAX_CTAS  64
+struct kllm_p2p_args {
+	uint8_t *const *peers;    /* device array [nranks]: every rank's exchange buffer */
+	int rank, nranks;
+	unsigned epoch;           /* 1, 2, ... per call, identical on every rank */
+	int num_rows, max_rows, head_dim;
+	const float *m, *l, *o;   /* this rank's triples (m natural-log domain) */
+	void *out;                /* bf16 [num_rows][head_dim] */
+	uint32_t *err;
+	uint64_t timeout_ns;
+};
+size_t kllm_p2p_buffer_bytes(int max_rows, int head_dim);
+int kllm_p2p_grid(int num_rows);
+int kllm_p2p_merge_launch(const struct kllm_p2p_args *a, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -64,6 +64,12 @@ struct kllm_gpu_ctx {
 	ncclComm_t comm;
 	int nranks, rank;
 	float *comm_recv;   /* m [nranks][rows], l [nranks][rows], o [nranks][rows][D] */
+	/* peer-memory exchange */
+	uint8_t *p2p_buf;                        /* this rank's exchange buffer */
+	uint8_t *p2p_peer[KLLM_P2P_MAX_RANKS];   /* every rank's, as mapped here */
+	uint8_t **p2p_peers_dev;                 /* the same table in device memory */
+	int p2p_max_rows, p2p_head_dim, p2p_nranks, p2p_rank;
+	unsigned p2p_epoch;
 };
 
 static int fail(struct kllm_gpu_ctx *ctx, int code)
@@ -196,6 +202,7 @@ void kllm_gpu_destroy(struct kllm_gpu_ctx *ctx)
 		cudaSetDevice(ctx->device);
 		cudaStreamSynchronize(ctx->stream);
 		kllm_gpu_comm_destroy(ctx);
+		kllm_gpu_p2p_destroy(ctx);
 		cudaFree(ctx->ws_part);
 		cudaFree(ctx->ws_cnt);
 		cudaStreamDestroy(ctx->stream);
@@ -963,4 +970,123 @@ void kllm_gpu_comm_destroy(struct kllm_gpu_ctx *ctx)
 	if (ctx->comm_recv)
 		cudaFree(ctx->comm_recv);
 	ctx->comm_recv = NULL;
+}
+
+/* ---- peer-memory split-KV exchange ---------------------------------------- */
+
+int kllm_gpu_p2p_export(struct kllm_gpu_ctx *ctx, int max_rows, int head_dim,
+			uint8_t handle[KLLM_P2P_HANDLE_BYTES])
+{
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (!handle || max_rows <= 0 || max_rows > 65536 || (head_dim != 64 && head_dim != 128) ||
+	    ctx->p2p_buf)
+		return fail(ctx, KLLM_EINVAL);
+	const int rows = (max_rows + 3) & ~3;   /* 16-byte aligned rows of the slots */
+	const size_t bytes = kllm_p2p_buffer_bytes(rows, head_dim);
+	cudaError_t e = cudaMalloc((void **)&ctx->p2p_buf, bytes);
+	if (e != cudaSuccess) {
+		ctx->p2p_buf = NULL;
+		return cuda_fail(ctx, e);
+	}
+	e = cudaMemset(ctx->p2p_buf, 0, bytes);
+	cudaIpcMemHandle_t h;
+	if (e == cudaSuccess)
+		e = cudaIpcGetMemHandle(&h, ctx->p2p_buf);
+	if (e != cudaSuccess) {
+		cudaFree(ctx->p2p_buf);
+		ctx->p2p_buf = NULL;
+		return cuda_fail(ctx, e);
+	}
+	memcpy(handle, &h, KLLM_P2P_HANDLE_BYTES);
+	ctx->p2p_max_rows = rows;
+	ctx->p2p_head_dim = head_dim;
+	ctx->p2p_epoch = 0;
+	return KLLM_OK;
+}
+
+int kllm_gpu_p2p_import(struct kllm_gpu_ctx *ctx, int nranks, int rank,
+			const uint8_t *handles)
+{
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (!ctx->p2p_buf || !handles || nranks < 1 || nranks > KLLM_P2P_MAX_RANKS || rank < 0 ||
+	    rank >= nranks || ctx->p2p_peers_dev)
+		return fail(ctx, KLLM_EINVAL);
+	memset(ctx->p2p_peer, 0, sizeof(ctx->p2p_peer));
+	for (int q = 0; q < nranks; ++q) {
+		if (q == rank) {
+			ctx->p2p_peer[q] = ctx->p2p_buf;
+			continue;
+		}
+		cudaIpcMemHandle_t h;
+		memcpy(&h, handles + (size_t)q * KLLM_P2P_HANDLE_BYTES, KLLM_P2P_HANDLE_BYTES);
+		void *p = NULL;
+		cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+		if (e != cudaSuccess) {
+			for (int k = 0; k < q; ++k)
+				if (k != rank && ctx->p2p_peer[k])
+					cudaIpcCloseMemHandle(ctx->p2p_peer[k]);
+			memset(ctx->p2p_peer, 0, sizeof(ctx->p2p_peer));
+			return cuda_fail(ctx, e);
+		}
+		ctx->p2p_peer[q] = (uint8_t *)p;
+	}
+	cudaError_t e = cudaMalloc((void **)&ctx->p2p_peers_dev, sizeof(uint8_t *) * nranks);
+	if (e == cudaSuccess)
+		e = cudaMemcpy(ctx->p2p_peers_dev, ctx->p2p_peer, sizeof(uint8_t *) * nranks,
+			       cudaMemcpyHostToDevice);
+	if (e != cudaSuccess)
+		return cuda_fail(ctx, e);
+	ctx->p2p_nranks = nranks;
+	ctx->p2p_rank = rank;
+	return KLLM_OK;
+}
+
+int kllm_gpu_p2p_merge(struct kllm_gpu_ctx *ctx, const float *m, const float *l,
+		       const float *o, int num_rows, int head_dim, void *out,
+		       uint32_t *err_word, int timeout_ms, void *stream)
+{
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (!ctx->p2p_peers_dev || !m || !l || !o || !out || num_rows <= 0 ||
+	    num_rows > ctx->p2p_max_rows || head_dim != ctx->p2p_head_dim ||
+	    ((uintptr_t)o & 15u))
+		return fail(ctx, KLLM_EINVAL);
+	struct kllm_p2p_args a;
+	memset(&a, 0, sizeof(a));
+	a.peers = ctx->p2p_peers_dev;
+	a.rank = ctx->p2p_rank;
+	a.nranks = ctx->p2p_nranks;
+	a.epoch = ++ctx->p2p_epoch;
+	a.num_rows = num_rows;
+	a.max_rows = ctx->p2p_max_rows;
+	a.head_dim = head_dim;
+	a.m = m;
+	a.l = l;
+	a.o = o;
+	a.out = out;
+	a.err = err_word;
+	a.timeout_ns = (uint64_t)(timeout_ms > 0 ? timeout_ms : 2000) * 1000000ull;
+	if (kllm_p2p_merge_launch(&a, pick_stream(ctx, stream)))
+		return cuda_fail(ctx, cudaErrorLaunchFailure);
+	ctx->stats.launches++;
+	return KLLM_OK;
+}
+
+void kllm_gpu_p2p_destroy(struct kllm_gpu_ctx *ctx)
+{
+	if (!ctx)
+		return;
+	for (int q = 0; q < KLLM_P2P_MAX_RANKS; ++q)
+		if (ctx->p2p_peer[q] && ctx->p2p_peer[q] != ctx->p2p_buf)
+			cudaIpcCloseMemHandle(ctx->p2p_peer[q]);
+	memset(ctx->p2p_peer, 0, sizeof(ctx->p2p_peer));
+	if (ctx->p2p_peers_dev)
+		cudaFree(ctx->p2p_peers_dev);
+	if (ctx->p2p_buf)
+		cudaFree(ctx->p2p_buf);
+	ctx->p2p_peers_dev = NULL;
+	ctx->p2p_buf = NULL;
+	ctx->p2p_nranks = 0;
 }

@@ -115,6 +115,11 @@ _SIGNATURES = [
     ("kllm_gpu_comm_merge", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int]),
     ("kllm_gpu_comm_destroy", None, [c_void_p]),
+    ("kllm_gpu_p2p_export", c_int, [c_void_p, c_int, c_int, POINTER(c_uint8)]),
+    ("kllm_gpu_p2p_import", c_int, [c_void_p, c_int, c_int, POINTER(c_uint8)]),
+    ("kllm_gpu_p2p_merge", c_int,
+     [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    ("kllm_gpu_p2p_destroy", None, [c_void_p]),
 ]
 
 _LIB = None
