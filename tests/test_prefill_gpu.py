@@ -114,7 +114,7 @@ def _check(got, want, what):
 
 
 @pytest.mark.parametrize("kv", [wl.KV_MX_FP8, wl.KV_BF16])
-@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 16), (64, 8)])
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 16), (64, 8), (16, 8)])
 def test_prefill_small(be, kv, hq, hkv):
     cfg = replace(wl.C2, kv_dtype=kv, hq=hq, hkv=hkv, mult_lo=None, mult_hi=None)
     case = _case(cfg, ctx_lens=[0, 37, 300, 128], chunk_lens=[200, 70, 33, 129])
