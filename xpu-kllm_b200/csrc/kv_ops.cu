@@ -29,19 +29,6 @@ __device__ __forceinline__ size_t section_bytes(int kv_dtype, int bs, int d)
 	return (size_t)bs * d * 2;
 }
 
-// E4M3 code -> float, the reference decoder's values
-// (userspace/compute/mx_dequant.h:30-55; 0x7F -> 480).
-__device__ __forceinline__ float e4m3_value(uint32_t code)
-{
-	const uint32_t e = (code >> 3) & 0xFu, m = code & 0x7u;
-	float v;
-	if (e != 0)
-		v = __uint_as_float(((e + 120u) << 23) | (m << 20));
-	else
-		v = (float)m * 0.001953125f;  // m * 2^-9
-	return (code & 0x80u) ? -v : v;
-}
-
 // Two floats -> two E4M3 codes, round to nearest even, saturate to +-448.
 // Returns lo in byte 0 and hi in byte 1.
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi)
@@ -49,21 +36,6 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi)
 	uint16_t r;
 	asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
 	return r;
-}
-
-// Smallest E4M3 code >= amax / 448 (the reference quantizer's scale rule,
-// mx_dequant.h:119-120, with a real E4M3 encoding in place of its stub).
-__device__ __forceinline__ uint32_t mx_scale_code(float amax)
-{
-	if (!(amax > 0.f))
-		return 0u;
-	const float t = __fdiv_rn(amax, 448.0f);
-	if (t > 448.0f)
-		return 0x7Eu;
-	uint32_t c = cvt_e4m3x2(t, 0.f) & 0xFFu;
-	if (e4m3_value(c) < t)
-		++c;
-	return c == 0u ? 1u : c;
 }
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -78,12 +50,67 @@ __device__ __forceinline__ uint4 append_load(const kllm_append_args &a, int i, i
 	    (((size_t)i * a.num_kv_heads + h) * a.head_dim + (size_t)b * 8) * 2);
 }
 
+// Tables for the MX quantizer, built at compile time: v[c] = value of E4M3
+// code c (the reference decoder's values), v[256 + c] = its reciprocal
+// rounded to nearest (compile-time float division is correctly rounded).
+struct E4m3Tables {
+	float v[512];
+};
+
+constexpr float e4m3_value_host(int code)
+{
+	const int e = (code >> 3) & 0xF, m = code & 7;
+	float scale = 1.0f;   // 2^(e - 10) for e > 0, 2^-9 for e == 0
+	const int ex = e ? e - 10 : -9;
+	for (int i = 0; i < (ex < 0 ? -ex : ex); ++i)
+		scale = ex < 0 ? scale * 0.5f : scale * 2.0f;
+	const float v = e ? (float)(8 + m) * scale : (float)m * scale;
+	return (code & 0x80) ? -v : v;
+}
+
+constexpr E4m3Tables make_e4m3_tables()
+{
+	E4m3Tables t{};
+	for (int i = 0; i < 256; ++i) {
+		t.v[i] = e4m3_value_host(i);
+		t.v[256 + i] = t.v[i] != 0.0f ? 1.0f / t.v[i] : 0.0f;
+	}
+	return t;
+}
+
+__device__ const E4m3Tables g_e4m3 = make_e4m3_tables();
+
+// Smallest E4M3 code >= amax / 448 (the reference quantizer's scale rule,
+// mx_dequant.h:119-120, with a real E4M3 encoding in place of its stub).
+// t = amax / 448 through the correctly rounded
+// reciprocal and one residual step, which is exact whenever the quotient is
+// representable; an E4M3 value can only equal RN(amax / 448) when amax / 448
+// is exactly that value (a bf16 and 448 x an E4M3 value differ by at least
+// 2^-8 relative otherwise), so the code is the one of exact division.
+__device__ __forceinline__ uint32_t mx_scale_code_tab(float amax, const float *tab)
+{
+	if (!(amax > 0.f))
+		return 0u;
+	constexpr float r448 = 1.0f / 448.0f;
+	const float q0 = amax * r448;
+	const float t = fmaf(fmaf(-448.0f, q0, amax), r448, q0);
+	if (t > 448.0f)
+		return 0x7Eu;
+	uint32_t c = cvt_e4m3x2(t, 0.f) & 0xFFu;
+	if (__ldg(&tab[c]) < t)
+		++c;
+	return c == 0u ? 1u : c;
+}
+
 // Writes micro-block x (b of kv head h, K or V) to position pos of sequence
 // seq: bf16 copy, MX-FP8 quantization, or the reference's BF16-payload form.
-__device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x, int seq,
-					     int pos, int h, int kv, int b)
+__device__ __forceinline__ void append_store(const kllm_append_args &a, const float *tab,
+					     uint4 x, int seq, int pos, int h, int kv, int b)
 {
-	const int blk = pos >= 0 ? pos / a.block_size : -1;
+	const int bs = a.block_size;
+	const bool pow2 = (bs & (bs - 1)) == 0;
+	const int lg = __ffs(bs) - 1;
+	const int blk = pos >= 0 ? (pow2 ? pos >> lg : pos / bs) : -1;
 	if (seq < 0 || seq >= a.num_seqs || blk < 0 || blk >= a.max_blocks) {
 		if (a.err && b == 0)
 			atomicOr(a.err, 0x4u);
@@ -97,8 +124,8 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x,
 			atomicOr(a.err, 0x4u);
 		return;
 	}
-	const int slot = pos - blk * a.block_size;
-	const int d = a.head_dim, bs = a.block_size;
+	const int slot = pos - blk * bs;
+	const int d = a.head_dim;
 	uint8_t *sec = reinterpret_cast<uint8_t *>(base) + a.layer_off +
 		       (size_t)h * section_bytes(a.kv_dtype, bs, d);
 
@@ -114,7 +141,7 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x,
 		amax = fmaxf(amax, fabsf(f[k]));
 
 	if (a.kv_dtype == 1) {
-		const uint32_t code = mx_scale_code(amax);
+		const uint32_t code = mx_scale_code_tab(amax, tab);
 		uint32_t lo = 0u, hi = 0u;
 		if (code != 0u) {
 			// x / s through the correctly rounded reciprocal plus one residual
@@ -123,8 +150,8 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x,
 			// such an exact quotient or at least 2^-9 (relative) away from every
 			// E4M3 rounding midpoint, so the E4M3 rounding below equals that of
 			// the correctly rounded quotient.
-			const float s = e4m3_value(code);
-			const float y = __frcp_rn(s);
+			const float s = __ldg(&tab[code]);
+			const float y = __ldg(&tab[256 + code]);
 			float q[8];
 #pragma unroll
 			for (int k = 0; k < 8; ++k) {
@@ -170,8 +197,8 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, uint4 x,
 // are in flight per thread and a warp reads 512 contiguous bytes per token.
 constexpr int kTokensPerCta = 4;
 
-__device__ __forceinline__ void append_tokens(const kllm_append_args &a, int i0,
-					      const int *seqs, const int *poss)
+__device__ __forceinline__ void append_tokens(const kllm_append_args &a, const float *tab,
+					      int i0, const int *seqs, const int *poss)
 {
 	const int nb = a.head_dim >> 3;
 	const int per_kv = a.num_kv_heads * nb;
@@ -189,11 +216,12 @@ __device__ __forceinline__ void append_tokens(const kllm_append_args &a, int i0,
 #pragma unroll
 	for (int t = 0; t < kTokensPerCta; ++t)
 		if (i0 + t < a.num_tokens)
-			append_store(a, x[t], seqs[t], poss[t], h, kv, b);
+			append_store(a, tab, x[t], seqs[t], poss[t], h, kv, b);
 }
 
 __global__ void __launch_bounds__(256) append_kernel(const kllm_append_args a)
 {
+	const float *tab = g_e4m3.v;
 	const int i0 = blockIdx.x * kTokensPerCta;
 	int seqs[kTokensPerCta], poss[kTokensPerCta];
 #pragma unroll
@@ -202,7 +230,7 @@ __global__ void __launch_bounds__(256) append_kernel(const kllm_append_args a)
 		seqs[t] = in ? a.token_seq[i0 + t] : -1;
 		poss[t] = in ? a.token_pos[i0 + t] : -1;
 	}
-	append_tokens(a, i0, seqs, poss);
+	append_tokens(a, tab, i0, seqs, poss);
 }
 
 // Same, with the (sequence, position) of row i derived from chunk offsets.
@@ -210,6 +238,7 @@ __global__ void __launch_bounds__(256) append_chunk_kernel(const kllm_append_arg
 							   const int *cu, const int *ctx)
 {
 	__shared__ int s_seq[kTokensPerCta], s_pos[kTokensPerCta];
+	const float *tab = g_e4m3.v;
 	const int i0 = blockIdx.x * kTokensPerCta;
 	if (threadIdx.x < kTokensPerCta) {
 		const int i = i0 + threadIdx.x;
@@ -226,7 +255,7 @@ __global__ void __launch_bounds__(256) append_chunk_kernel(const kllm_append_arg
 		s_pos[threadIdx.x] = in ? ctx[lo] + (i - cu[lo]) : -1;
 	}
 	__syncthreads();
-	append_tokens(a, i0, s_seq, s_pos);
+	append_tokens(a, tab, i0, s_seq, s_pos);
 }
 
 // One warp per (seq, kv head): walk the pages in order, skip invalid
