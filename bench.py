@@ -785,6 +785,316 @@ def run_reference_prefill(args) -> None:
 # reference arm (CPU)
 # ---------------------------------------------------------------------------
 
+TABLE_METRIC = ("content-addressed block-table build (SHA-256 block key + index probe + "
+                "24-byte entry): table blocks/s")
+
+
+def chained_keys(tokens: np.ndarray, lens: np.ndarray, starts: np.ndarray, block: int):
+    """Host block keys with hashlib, one running hash per sequence (the same
+    values as hashing every prefix from scratch)."""
+    import hashlib
+    keys = []
+    for s, n in enumerate(lens.tolist()):
+        h = hashlib.sha256()
+        seq = tokens[starts[s]:starts[s] + n]
+        row = []
+        for b in range((n + block - 1) // block):
+            h.update(seq[b * block:(b + 1) * block].tobytes())
+            row.append(h.copy().digest())
+        keys.append(row)
+    return keys
+
+
+class TableRig:
+    """A table-build workload resident on the GPU: token ids, the index mirror
+    (warm: every block indexed; prefix: the shared prefix chain only), the
+    table, keys, workspace and miss list."""
+
+    def __init__(self, tcfg, be, torch, device: int, seed: int = 0):
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import tablecase as tc
+        self.tcfg, self.be, self.torch = tcfg, be, torch
+        c = tcfg.lengths
+        self.block = c.block
+        self.tokens, self.starts, self.lens = wl.table_tokens(tcfg, seed)
+        S = len(self.lens)
+        nb = (self.lens + self.block - 1) // self.block
+        self.blocks = int(nb.sum())
+        self.max_blocks = int(nb.max())
+        if tcfg.warm == "prefix":
+            ctx, chunk = wl.prefill_split(c)
+            self.plan = wl.plan_prefill_pages(c, ctx, chunk, seed)
+            indexed = [(s, b) for s in range(S) if ctx[s] for b in range(int(ctx[s]) // c.block)]
+        else:
+            self.plan = wl.plan_pages(c, self.lens, seed)
+            indexed = [(s, b) for s in range(S) for b in range(int(nb[s]))]
+        keys = chained_keys(self.tokens, self.lens, self.starts, self.block)
+        self.entries = tc.empty_index(tcfg.index_capacity)
+        seen = set()
+        for s, b in indexed:
+            k = keys[s][b]
+            if k not in seen:
+                seen.add(k)
+                tc.index_insert(self.entries, k, int(self.plan.slots[s, b]))
+        self.expected_hits = len(indexed)
+        self.base = 0x7f0000000000
+        self.slot_bytes = c.slot_bytes()
+        self.want_table = wl.block_table(self.plan, c, self.base)
+        if tcfg.warm == "prefix":
+            hit = np.zeros(self.plan.slots.shape, bool)
+            for s, b in indexed:
+                hit[s, b] = True
+            self.want_table[~hit] = 0
+        dev = torch.device("cuda", device)
+        self.d_tokens = torch.from_numpy(self.tokens.view(np.int32)).to(dev)
+        self.d_starts = torch.from_numpy(self.starts).to(dev)
+        self.d_lens = torch.from_numpy(self.lens).to(dev)
+        self.d_index = torch.from_numpy(self.entries.view(np.uint8).copy()).to(dev)
+        self.table = torch.zeros(S * self.max_blocks * 24, dtype=torch.uint8, device=dev)
+        self.hashes = torch.zeros(S * self.max_blocks * 32, dtype=torch.uint8, device=dev)
+        self.ws_bytes = be.lib.kllm_gpu_table_workspace_size(S, self.max_blocks, self.block)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.miss_list = torch.zeros(2 * self.blocks, dtype=torch.int32, device=dev)
+        self.miss_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.hit_miss = torch.zeros(2, dtype=torch.int64, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def build(self, stream: int, tokens=None, starts=None, lens=None) -> None:
+        rc = self.be.build_tables(
+            token_ids=tokens or self.d_tokens.data_ptr(),
+            token_starts=starts or self.d_starts.data_ptr(),
+            seq_lens=lens or self.d_lens.data_ptr(), first_block=None,
+            num_seqs=len(self.lens), max_blocks_per_seq=self.max_blocks, block_size=self.block,
+            index=self.d_index.data_ptr(), index_capacity=self.tcfg.index_capacity, now_ns=0,
+            arena_base=self.base, slot_bytes=self.slot_bytes, total_slots=self.plan.n_slots,
+            k_offset=0, v_offset=self.tcfg.lengths.page_bytes(),
+            block_tables=self.table.data_ptr(), hashes=self.hashes.data_ptr(),
+            workspace=self.ws.data_ptr(), workspace_bytes=self.ws_bytes,
+            miss_list=self.miss_list.data_ptr(), miss_capacity=self.blocks,
+            miss_count=self.miss_count.data_ptr(), hit_miss=self.hit_miss.data_ptr(),
+            err_word=self.err.data_ptr(), stream=stream)
+        if rc != 0:
+            raise RuntimeError(f"block-table build failed: {rc}")
+
+    def check(self) -> None:
+        """The table equals the planned one (warm: every block; prefix: the
+        shared chain), the miss count is the unindexed blocks."""
+        self.torch.cuda.synchronize()
+        got = self.table.cpu().numpy().view(wl.ENTRY_DTYPE).reshape(self.want_table.shape)
+        assert (got == self.want_table).all(), "block-table build differs from the plan"
+        assert int(self.miss_count.item()) == self.blocks - self.expected_hits
+        assert int(self.err.item()) == 0
+
+    def algorithmic_bytes(self) -> int:
+        """Token ids read once, one index entry (48 B) per block, table and
+        keys written ([S][max_blocks]), midstates written and read once."""
+        S = len(self.lens)
+        msg_blocks = int((self.lens // 16).sum())
+        return (4 * int(self.lens.sum()) + 48 * self.blocks +
+                (24 + 32) * S * self.max_blocks + 64 * msg_blocks + 12 * S)
+
+
+def run_tables(args) -> None:
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ["KLLM_GPU_DEVICE"] = str(local)
+    import kllm_b200 as kb
+    be = kb.Backend()
+    if be.backend != kb.KLLM_GPU_CUDA:
+        raise RuntimeError("libkllm_gpu: no sm_100 device")
+    torch.cuda.set_stream(be.torch_stream())
+    tcfg = wl.TABLE_CONFIGS[args.config]
+    rig = TableRig(tcfg, be, torch, local, args.seed)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    for _ in range(args.warmup):
+        rig.build(sp)
+    rig.check()
+    # the workload (~25-60 MB) fits in L2: every timed build follows a
+    # 256 MB write that flushes it
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+    clk = Clocks(local)
+    clk.start()
+    launches0 = be.stats().launches
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        evs[2 * i].record(stream)
+        rig.build(sp)
+        evs[2 * i + 1].record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = be.stats().launches - launches0
+    times = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(args.steps)]
+    t_ms = float(sum(times))
+
+    # end to end through the C ABI: pinned host token ids / starts / lengths
+    # in, the build, the miss count and hit/miss counters back
+    h_tok = torch.from_numpy(rig.tokens.view(np.int32)).pin_memory()
+    h_st = torch.from_numpy(rig.starts).pin_memory()
+    h_ln = torch.from_numpy(rig.lens).pin_memory()
+    h_out = torch.zeros(6, dtype=torch.int32).pin_memory()
+    d_tok, d_st, d_ln = (torch.empty_like(x, device=f"cuda:{local}") for x in (h_tok, h_st, h_ln))
+    lib, ctx = be.lib, be.ctx
+    h2d = [(d_tok, h_tok, rig.tokens.nbytes), (d_st, h_st, rig.starts.nbytes),
+           (d_ln, h_ln, rig.lens.nbytes)]
+
+    def e2e_step():
+        for d, h, n in h2d:
+            lib.kllm_gpu_memcpy_h2d_async(ctx, d.data_ptr(), h.data_ptr(), n, sp)
+        rig.build(sp, d_tok.data_ptr(), d_st.data_ptr(), d_ln.data_ptr())
+        lib.kllm_gpu_memcpy_d2h_async(ctx, h_out.data_ptr(), rig.miss_count.data_ptr(), 4, sp)
+        lib.kllm_gpu_memcpy_d2h_async(ctx, h_out[2:].data_ptr(), rig.hit_miss.data_ptr(), 16, sp)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_ms = 0.0
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms += e0.elapsed_time(e1)
+    assert int(h_out[0]) == rig.blocks - rig.expected_hits
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = table_cpu_sample(rig, args.cpu_seconds)
+    if rank == 0:
+        hpeak, hkind = peaks()
+        per_ms = t_ms / args.steps
+        gbs = rig.algorithmic_bytes() / (per_ms * 1e-3) / 1e9
+        longest = int(rig.lens.max()) // 16
+        line = {
+            "metric": TABLE_METRIC,
+            "value": round(rig.blocks * args.steps / (t_ms * 1e-3), 1), "unit": "blocks/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32",
+            "data": "synthetic (seeded token ids in [0, 128256))",
+            "config": {"workload": tcfg.name, "requests": len(rig.lens),
+                       "tokens": int(rig.lens.sum()), "table_blocks": rig.blocks,
+                       "block": rig.block, "index_capacity": tcfg.index_capacity,
+                       "indexed_blocks": rig.expected_hits,
+                       "l2": "flushed before every timed build (256 MB write)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hpeak,
+                         "unit": "GB/s", "frac": round(gbs / hpeak, 5), "peak_kind": hkind,
+                         "traffic": None,
+                         "kernel": "chain_kernel + finalize_kernel (one build)",
+                         "note": "latency-bound: the SHA-256 chain of a sequence is "
+                                 "sequential; the longest request has "
+                                 f"{longest} 64-byte message blocks",
+                         "chain_message_blocks_longest": longest},
+            "e2e": {"value": round(rig.blocks * args.steps / (e_ms * 1e-3), 1),
+                    "unit": "blocks/s",
+                    "h2d_bytes_per_step": int(sum(n for _, _, n in h2d)),
+                    "d2h_bytes_per_step": 20},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
+    be.close()
+
+
+class RefTables:
+    """The reference's path on a table workload: its own index (cache_index.c)
+    holding the same keys, OpenSSL SHA256 of every block's prefix spread over
+    host threads, then kllm_index_lookup per block on one thread."""
+
+    def __init__(self, tcfg, seed: int, nthreads: int):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        self.ok = oracle.ref_index_lib() is not None
+        self.tokens, self.starts, self.lens = wl.table_tokens(tcfg, seed)
+        c = tcfg.lengths
+        self.block, self.nthreads = c.block, nthreads
+        nb = (self.lens + c.block - 1) // c.block
+        self.blocks, self.max_blocks = int(nb.sum()), int(nb.max())
+        if not self.ok:
+            return
+        keys = chained_keys(self.tokens, self.lens, self.starts, c.block)
+        if tcfg.warm == "prefix":
+            ctx, _ = wl.prefill_split(c)
+            indexed = {keys[s][b] for s in range(len(self.lens)) if ctx[s]
+                       for b in range(int(ctx[s]) // c.block)}
+        else:
+            indexed = {k for row in keys for k in row}
+        self.expected_hits = sum(1 for row in keys for k in row if k in indexed)
+        self.idx = oracle.RefIndex(tcfg.index_capacity, 1 << 22)
+        for k in sorted(indexed):
+            self.idx.insert(k)
+
+    def run(self):
+        """(key seconds, lookup seconds) of one build; checks the hit count."""
+        slots, _, tk, tl = self.idx.build_slots_mt(self.tokens, self.starts, self.lens,
+                                                   self.max_blocks, self.block, self.nthreads)
+        assert int((slots >= 0).sum()) == self.expected_hits
+        return tk, tl
+
+
+def table_cpu_sample(rig, seconds: float) -> dict | None:
+    n = os.cpu_count() or 1
+    ref = RefTables(rig.tcfg, 0, n)
+    if not ref.ok:
+        return None
+    t0 = time.perf_counter()
+    reps, tk, tl = 0, 0.0, 0.0
+    while reps < 200:
+        a, b = ref.run()
+        reps, tk, tl = reps + 1, tk + a, tl + b
+        if time.perf_counter() - t0 > min(seconds, 10.0):
+            break
+    per = (tk + tl) / reps
+    return {"value": round(ref.blocks / per, 1), "unit": "blocks/s", "cores": n,
+            "kind": "reference", "key_seconds": round(tk / reps, 6),
+            "lookup_seconds": round(tl / reps, 6),
+            "sample": f"the whole workload x {reps} reps: OpenSSL SHA256 of every "
+                      f"block's prefix over {n} threads, then kllm_index_lookup on one"}
+
+
+def run_reference_tables(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    tcfg = wl.TABLE_CONFIGS[args.config]
+    n = os.cpu_count() or 1
+    ref = RefTables(tcfg, args.seed, n)
+    if not ref.ok:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libkllm_ref_index.so was not built here"}), flush=True)
+        return
+    for _ in range(args.warmup):
+        ref.run()
+    t = sum(sum(ref.run()) for _ in range(args.steps))
+    value = ref.blocks * args.steps / t
+    line = {
+        "impl": "reference", "metric": TABLE_METRIC, "value": round(value, 1),
+        "unit": "blocks/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+        "config": {"workload": tcfg.name, "block": tcfg.lengths.block,
+                   "index_capacity": tcfg.index_capacity},
+        "cpu_baseline": {"value": round(value, 1), "unit": "blocks/s", "cores": n,
+                         "kind": "reference",
+                         "sample": "the whole workload per step: OpenSSL SHA256 of every "
+                                   f"block's prefix over {n} threads, then kllm_index_lookup"},
+        "e2e": {"value": round(value, 1), "unit": "blocks/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -845,7 +1155,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
     ap.add_argument("--config", default=wl.C3.name,
-                    choices=list(wl.CONFIGS) + list(wl.PREFILL_CONFIGS))
+                    choices=list(wl.CONFIGS) + list(wl.PREFILL_CONFIGS) +
+                    list(wl.TABLE_CONFIGS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -862,6 +1173,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     prefill = args.config in wl.PREFILL_CONFIGS
+    if args.config in wl.TABLE_CONFIGS:
+        (run_reference_tables if args.impl == "reference" else run_tables)(args)
+        return
     if args.impl == "reference":
         (run_reference_prefill if prefill else run_reference)(args)
     else:

@@ -377,6 +377,71 @@ int kllm_gpu_comm_merge(struct kllm_gpu_ctx *ctx, const float *m,
 			int head_dim, void *out, void *stream, int timeout_ms);
 void kllm_gpu_comm_destroy(struct kllm_gpu_ctx *ctx);
 
+/* Content-addressed block-table build on the GPU (the reference does this on
+ * the host per block: userspace/compute/infer_gpu.c:110-118 computes the
+ * block key, userspace/kvcache/cache_index.c:87-108 looks it up,
+ * userspace/kvcache/arena_alloc.c:196-201 maps the slot to its page).
+ *
+ * Block b of sequence s has the key SHA-256(token_ids[0, min((b+1) *
+ * block_size, seq_len)) as little-endian uint32), looked up in a device
+ * mirror of the cache index with the reference's probe: bucket = first four
+ * key bytes (little-endian) & (capacity - 1), linear probing that stops at
+ * the first empty entry (slot_index 0xFFFFFFFF), full 32-byte match. A hit
+ * writes the entry {arena_base + slot * slot_bytes + k_offset, ... +
+ * v_offset, valid = 1} (valid = 0 when slot >= total_slots) and, when
+ * now_ns != 0, stamps the index entry's last_access_ns; a miss writes a zero
+ * entry and is counted and listed. Blocks in [ceil(len / block_size),
+ * max_blocks_per_seq) get zero entries; a sequence longer than the table is
+ * cut at max_blocks_per_seq * block_size tokens and flagged with
+ * KLLM_ERR_SEQ_TOO_LONG.
+ *
+ * Incremental use: with first_block, blocks below first_block[s] are left
+ * untouched and the hash chain restarts from the state the workspace kept;
+ * first_block[s] * block_size must not exceed the tokens of sequence s that
+ * an earlier call with the same workspace (same sequence row) covered, and
+ * those tokens must be unchanged. */
+struct kllm_gpu_index_entry {           /* userspace/kvcache/cache_index.h:22-27 */
+	uint8_t hash[32];
+	uint32_t slot_index;                /* 0xFFFFFFFF: empty */
+	uint32_t flags;
+	uint64_t last_access_ns;
+};
+
+struct kllm_gpu_table_build_params {
+	uint32_t struct_size;
+	uint32_t flags;
+	const uint32_t *token_ids;   /* packed token ids of all sequences */
+	const int64_t *token_starts; /* [num_seqs]: index of sequence s's first token */
+	const int *seq_lens;         /* [num_seqs] */
+	const int *first_block;      /* [num_seqs] or NULL (all 0) */
+	int num_seqs;
+	int max_blocks_per_seq;
+	int block_size;              /* tokens per block */
+	struct kllm_gpu_index_entry *index; /* [index_capacity], 16-byte aligned */
+	uint32_t index_capacity;     /* power of two */
+	uint64_t now_ns;             /* LRU stamp for hits; 0 leaves the index unchanged */
+	uint64_t arena_base;         /* device address of slot 0 */
+	uint64_t slot_bytes;
+	uint64_t total_slots;
+	uint64_t k_offset;           /* K page offset inside a slot */
+	uint64_t v_offset;           /* V page offset inside a slot */
+	void *block_tables;          /* out: kllm_block_table_entry [num_seqs][max_blocks_per_seq] */
+	uint8_t *hashes;             /* out, optional: [num_seqs][max_blocks_per_seq][32], 16-byte aligned */
+	void *workspace;             /* kllm_gpu_table_workspace_size bytes, 16-byte aligned */
+	uint64_t workspace_bytes;
+	int *miss_list;              /* out, optional: (seq, block) int pairs, unordered */
+	int miss_capacity;           /* pairs miss_list holds */
+	int *miss_count;             /* out, optional: misses of this call (may exceed miss_capacity) */
+	uint64_t *hit_miss;          /* optional: [2] += hits, misses (kllm_index_stats counters) */
+	uint32_t *err_word;
+	void *stream;
+};
+
+uint64_t kllm_gpu_table_workspace_size(int num_seqs, int max_blocks_per_seq,
+				       int block_size);
+int kllm_gpu_build_block_tables(struct kllm_gpu_ctx *ctx,
+				const struct kllm_gpu_table_build_params *p);
+
 /* Cross-GPU split-KV exchange over peer memory (no counterpart in the
  * reference): the same result as kllm_gpu_comm_merge, computed by one kernel
  * per rank that stores this rank's triples into every peer's exchange

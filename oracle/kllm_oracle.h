@@ -120,6 +120,39 @@ int orc_causal_rows(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 		    uint16_t *out, int n_rows, int pos0, int group,
 		    int head_dim, float scale);
 
+/* ---- content-addressed block tables (content_index.c) -------------------- */
+
+/* Entry of the reference's cache index, same 48-byte layout
+ * (userspace/kvcache/cache_index.h:22-27). */
+#define ORC_INDEX_EMPTY 0xFFFFFFFFu  /* cache_index.c:16 EMPTY_SLOT */
+struct orc_index_entry {
+	uint8_t hash[32];
+	uint32_t slot_index;
+	uint32_t flags;
+	uint64_t last_access_ns;
+};
+
+/* SHA-256 (FIPS 180-4), the function the reference calls through OpenSSL. */
+void orc_sha256(const void *msg, size_t len, uint8_t out[32]);
+/* infer_gpu.c:110-118: SHA-256 of tokens[0, min((b+1)*block_size, seq_len)). */
+void orc_block_key(const uint32_t *tokens, int seq_len, int block_size, int b,
+		   uint8_t out[32]);
+/* cache_index.c:35-41, 87-108: position of the key's entry, or -1. */
+int64_t orc_index_probe(const struct orc_index_entry *entries, uint32_t capacity,
+			const uint8_t hash[32]);
+/* Content-addressed block-table build (key, probe, slot -> page pointers);
+ * table entries carry device addresses. Returns 1 if a sequence was cut at
+ * max_blocks * block_size tokens, else 0. */
+int orc_build_block_tables(const uint32_t *tokens, const int64_t *starts,
+			   const int32_t *seq_lens, const int32_t *first_block,
+			   int num_seqs, int max_blocks, int block_size,
+			   struct orc_index_entry *index, uint32_t capacity,
+			   uint64_t now_ns, uint64_t arena_base,
+			   uint64_t slot_bytes, uint64_t total_slots,
+			   uint64_t k_offset, uint64_t v_offset,
+			   struct orc_entry *table, uint8_t *hashes,
+			   uint64_t *hits, uint64_t *misses);
+
 #ifdef __cplusplus
 }
 #endif

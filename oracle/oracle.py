@@ -7,7 +7,10 @@ Loaded only by tests/, the smoke check and bench.py's CPU-baseline leg:
 * ``_ref/libkllm_ref_{avx512,scalar}.so``: the reference's own
   ``userspace/compute/ace_attention.c`` and ``mx_dequant.h`` compiled from
   its sources (oracle/Makefile), used to pin the restatement and as the
-  "reference" CPU baseline.
+  "reference" CPU baseline;
+* ``_ref/libkllm_ref_index.so``: the reference's own
+  ``userspace/kvcache/cache_index.c`` with OpenSSL's ``SHA256`` block key
+  (``userspace/compute/infer_gpu.c:110-118``), for the block-table build.
 """
 from __future__ import annotations
 
@@ -72,6 +75,17 @@ def _bind(lib, prefix):
     lib.orc_causal_rows.restype = c_int
     lib.orc_causal_rows.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                     c_int, c_float]
+    lib.orc_sha256.restype = None
+    lib.orc_sha256.argtypes = [c_void_p, ctypes.c_size_t, c_void_p]
+    lib.orc_block_key.restype = None
+    lib.orc_block_key.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p]
+    lib.orc_index_probe.restype = ctypes.c_int64
+    lib.orc_index_probe.argtypes = [c_void_p, c_uint32, c_void_p]
+    lib.orc_build_block_tables.restype = c_int
+    lib.orc_build_block_tables.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                           c_int, c_void_p, c_uint32, c_uint64, c_uint64,
+                                           c_uint64, c_uint64, c_uint64, c_uint64, c_void_p,
+                                           c_void_p, POINTER(c_uint64), POINTER(c_uint64)]
     h = getattr(lib, f"{prefix}_harness_paged_decode")
     h.restype = c_int
     h.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
@@ -132,6 +146,43 @@ def ref():
         lib.ref_ace_probe()
         _REF = lib
     return _REF
+
+
+_REF_INDEX = None
+
+
+def ref_index_lib():
+    """The reference's cache index + SHA256 block key (None when never built)."""
+    global _REF_INDEX
+    if _REF_INDEX is None:
+        p = os.path.join(REF_DIR, "libkllm_ref_index.so")
+        if not os.path.exists(p):
+            return None
+        lib = ctypes.CDLL(p)
+        lib.ref_index_new.restype = c_void_p
+        lib.ref_index_new.argtypes = [c_uint32, c_uint64]
+        lib.ref_index_free.restype = None
+        lib.ref_index_free.argtypes = [c_void_p]
+        for name in ("ref_index_insert", "ref_index_lookup"):
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int64
+            fn.argtypes = [c_void_p, c_void_p]
+        lib.ref_index_evict.restype = c_int
+        lib.ref_index_evict.argtypes = [c_void_p, c_void_p]
+        lib.ref_index_entries.restype = c_void_p
+        lib.ref_index_entries.argtypes = [c_void_p]
+        lib.ref_index_stats.restype = None
+        lib.ref_index_stats.argtypes = [c_void_p, c_void_p]
+        lib.ref_block_keys.restype = None
+        lib.ref_block_keys.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_void_p]
+        lib.ref_build_slots_mt.restype = c_int
+        lib.ref_build_slots_mt.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                           c_int, c_void_p, c_void_p, c_int, POINTER(c_double)]
+        lib.ref_build_slots.restype = None
+        lib.ref_build_slots.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                        c_int, c_void_p]
+        _REF_INDEX = lib
+    return _REF_INDEX
 
 
 def ptr(a: np.ndarray) -> int:
@@ -236,3 +287,139 @@ def harness_decode(lib, prefix, q, table, seq_lens, hq, hkv, d, max_blocks, scal
             scale, block, kv_dtype, layer_off, nthreads, times)
     assert rc == 0
     return out, times[0], times[1], times[2]
+
+
+# ---- content-addressed block tables -------------------------------------------
+
+# userspace/kvcache/cache_index.h:22-27
+INDEX_ENTRY = np.dtype([("hash", "u1", (32,)), ("slot_index", "<u4"), ("flags", "<u4"),
+                        ("last_access_ns", "<u8")])
+assert INDEX_ENTRY.itemsize == 48
+INDEX_EMPTY = 0xFFFFFFFF
+
+
+def sha256(msg: bytes) -> bytes:
+    buf = np.frombuffer(bytes(msg), dtype=np.uint8).copy() if msg else np.zeros(1, np.uint8)
+    out = np.zeros(32, dtype=np.uint8)
+    orc().orc_sha256(ptr(buf), len(msg), ptr(out))
+    return out.tobytes()
+
+
+def block_keys(tokens: np.ndarray, seq_len: int, block_size: int, n_blocks: int,
+               use_ref: bool = False) -> np.ndarray:
+    """[n_blocks][32] keys of one sequence (the reference's SHA256 call when use_ref)."""
+    tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+    if tok.size == 0:
+        tok = np.zeros(1, np.uint32)
+    out = np.zeros((n_blocks, 32), dtype=np.uint8)
+    if use_ref:
+        ref_index_lib().ref_block_keys(ptr(tok), seq_len, block_size, n_blocks, ptr(out))
+    else:
+        for b in range(n_blocks):
+            orc().orc_block_key(ptr(tok), seq_len, block_size, b, ptr(out[b]))
+    return out
+
+
+def index_probe(entries: np.ndarray, key) -> int:
+    e = np.ascontiguousarray(entries)
+    assert e.dtype == INDEX_ENTRY
+    k = np.frombuffer(bytes(key), dtype=np.uint8).copy()
+    return int(orc().orc_index_probe(ptr(e), len(e), ptr(k)))
+
+
+def build_block_tables(tokens, starts, seq_lens, index, *, max_blocks, block_size, arena_base,
+                       slot_bytes, total_slots, k_offset, v_offset, first_block=None,
+                       now_ns=0, table=None, hashes=None):
+    """orc_build_block_tables; index is updated in place (LRU stamps).
+    Returns (table [S][max_blocks] of 24-byte entries, hashes [S][max_blocks][32],
+    hits, misses, err)."""
+    tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+    if tok.size == 0:
+        tok = np.zeros(1, np.uint32)
+    st = np.ascontiguousarray(starts, dtype=np.int64)
+    ln = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    S = len(ln)
+    assert index.dtype == INDEX_ENTRY and index.flags["C_CONTIGUOUS"]
+    if table is None:
+        table = np.zeros(S * max_blocks * 24, dtype=np.uint8)
+    if hashes is None:
+        hashes = np.zeros((S, max_blocks, 32), dtype=np.uint8)
+    fb = None if first_block is None else np.ascontiguousarray(first_block, dtype=np.int32)
+    hits, misses = c_uint64(0), c_uint64(0)
+    err = orc().orc_build_block_tables(ptr(tok), ptr(st), ptr(ln), None if fb is None else ptr(fb),
+                                       S, max_blocks, block_size, ptr(index), len(index), now_ns,
+                                       arena_base, slot_bytes, total_slots, k_offset, v_offset,
+                                       ptr(table), ptr(hashes), ctypes.byref(hits),
+                                       ctypes.byref(misses))
+    return table, hashes, hits.value, misses.value, err
+
+
+class RefIndex:
+    """The reference's own cache index (cache_index.c) over a test arena."""
+
+    def __init__(self, capacity: int, total_slots: int):
+        self.lib = ref_index_lib()
+        if self.lib is None:
+            raise RuntimeError("oracle/_ref/libkllm_ref_index.so was not built")
+        self.h = self.lib.ref_index_new(capacity, total_slots)
+        if not self.h:
+            raise ValueError("kllm_index_create rejected the capacity")
+        self.capacity = capacity
+
+    def close(self):
+        if self.h:
+            self.lib.ref_index_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @staticmethod
+    def _key(key):
+        return np.frombuffer(bytes(key), dtype=np.uint8).copy()
+
+    def insert(self, key) -> int:
+        k = self._key(key)
+        return int(self.lib.ref_index_insert(self.h, ptr(k)))
+
+    def lookup(self, key) -> int:
+        k = self._key(key)
+        return int(self.lib.ref_index_lookup(self.h, ptr(k)))
+
+    def evict(self, key) -> bool:
+        k = self._key(key)
+        return bool(self.lib.ref_index_evict(self.h, ptr(k)))
+
+    def entries(self) -> np.ndarray:
+        """A copy of the index's entry array."""
+        p = self.lib.ref_index_entries(self.h)
+        raw = (ctypes.c_uint8 * (48 * self.capacity)).from_address(p)
+        return np.frombuffer(bytes(raw), dtype=INDEX_ENTRY).copy()
+
+    def stats(self) -> dict:
+        out = np.zeros(6, dtype=np.uint64)
+        self.lib.ref_index_stats(self.h, ptr(out))
+        return dict(zip(("hits", "misses", "evictions", "insertions", "occupied", "capacity"),
+                        (int(x) for x in out)))
+
+    def build_slots(self, tokens, starts, seq_lens, max_blocks, block_size) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        st = np.ascontiguousarray(starts, dtype=np.int64)
+        ln = np.ascontiguousarray(seq_lens, dtype=np.int32)
+        slots = np.zeros((len(ln), max_blocks), dtype=np.int64)
+        self.lib.ref_build_slots(self.h, ptr(tok), ptr(st), ptr(ln), len(ln), max_blocks,
+                                 block_size, ptr(slots))
+        return slots
+
+    def build_slots_mt(self, tokens, starts, seq_lens, max_blocks, block_size, nthreads):
+        """(slots, keys, key_seconds, lookup_seconds) of ref_build_slots_mt."""
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        st = np.ascontiguousarray(starts, dtype=np.int64)
+        ln = np.ascontiguousarray(seq_lens, dtype=np.int32)
+        slots = np.zeros((len(ln), max_blocks), dtype=np.int64)
+        keys = np.zeros((len(ln), max_blocks, 32), dtype=np.uint8)
+        t = (c_double * 2)()
+        rc = self.lib.ref_build_slots_mt(self.h, ptr(tok), ptr(st), ptr(ln), len(ln), max_blocks,
+                                         block_size, ptr(slots), ptr(keys), nthreads, t)
+        assert rc == 0
+        return slots, keys, t[0], t[1]

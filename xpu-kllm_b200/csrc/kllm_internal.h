@@ -18,6 +18,7 @@ extern "C" {
 #define KLLM_SLOT_FLOATS    1040  /* one split-KV partial: o[8][128], m[8], l[8] */
 #define KLLM_MAX_SEQS_LAUNCH 4096 /* sequences per decode launch (smem prefix) */
 
+#define KLLM_ERR_SEQ_TOO_LONG_BIT 0x1u /* seq_len beyond the table: clamped */
 #define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
 /* MX-FP8 decode computes with K/V values scaled by 2^-2 (payload x scale
  * stays below the f16 maximum); scores and outputs are multiplied back. */
@@ -132,6 +133,30 @@ struct kllm_p2p_args {
 size_t kllm_p2p_buffer_bytes(int max_rows, int head_dim);
 int kllm_p2p_grid(int num_rows);
 int kllm_p2p_merge_launch(const struct kllm_p2p_args *a, void *stream);
+
+/* Content-addressed block-table build (block_tables.cu). */
+struct kllm_table_args {
+	const uint32_t *tokens;   /* packed token ids */
+	const int64_t *starts;    /* [num_seqs] first token of each sequence */
+	const int *seq_lens;      /* [num_seqs] */
+	const int *first_block;   /* [num_seqs] or NULL */
+	int num_seqs, max_blocks, block_size;
+	uint8_t *index;           /* 48-byte entries [capacity], 16-byte aligned */
+	uint32_t capacity;        /* power of two */
+	unsigned long long now_ns;
+	unsigned long long arena_base, slot_bytes, total_slots, k_offset, v_offset;
+	void *table;              /* 24-byte entries [num_seqs][max_blocks] */
+	uint8_t *hashes;          /* [num_seqs][max_blocks][32] or NULL */
+	uint32_t *midstates;      /* [num_seqs][ms_stride][8] */
+	uint64_t ms_stride;
+	int *miss_list;           /* (seq, block) pairs or NULL */
+	int miss_capacity;
+	int *miss_count;          /* or NULL */
+	unsigned long long *hit_miss; /* [2] or NULL */
+	uint32_t *err;
+};
+uint64_t kllm_table_midstate_stride(int max_blocks, int block_size);
+int kllm_table_build_launch(const struct kllm_table_args *a, void *stream);
 
 #ifdef __cplusplus
 }

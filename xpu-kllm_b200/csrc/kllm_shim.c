@@ -781,6 +781,71 @@ int kllm_gpu_gather_debug(struct kllm_gpu_ctx *ctx,
 	return KLLM_OK;
 }
 
+uint64_t kllm_gpu_table_workspace_size(int num_seqs, int max_blocks_per_seq,
+				       int block_size)
+{
+	if (num_seqs < 0 || max_blocks_per_seq <= 0 || block_size <= 0)
+		return 0;
+	return (uint64_t)num_seqs *
+	       kllm_table_midstate_stride(max_blocks_per_seq, block_size) * 32u;
+}
+
+int kllm_gpu_build_block_tables(struct kllm_gpu_ctx *ctx,
+				const struct kllm_gpu_table_build_params *p)
+{
+	if (!p || p->struct_size < sizeof(*p))
+		return fail(ctx, KLLM_EINVAL);
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (p->num_seqs < 0 || p->max_blocks_per_seq <= 0 || p->block_size <= 0 ||
+	    p->miss_capacity < 0 || p->index_capacity == 0 ||
+	    (p->index_capacity & (p->index_capacity - 1)) ||
+	    (int64_t)p->max_blocks_per_seq * p->block_size > INT32_MAX)
+		return fail(ctx, KLLM_EINVAL);
+	if (p->num_seqs == 0)
+		return KLLM_OK;
+	if (!p->token_ids || !p->token_starts || !p->seq_lens || !p->index ||
+	    !p->block_tables || !p->workspace || (p->miss_capacity > 0 && !p->miss_list))
+		return fail(ctx, KLLM_EINVAL);
+	if (((uintptr_t)p->index | (uintptr_t)p->hashes | (uintptr_t)p->workspace) & 15u ||
+	    ((uintptr_t)p->block_tables & 7u) || ((uintptr_t)p->token_ids & 3u))
+		return fail(ctx, KLLM_EINVAL);
+	if (p->workspace_bytes < kllm_gpu_table_workspace_size(p->num_seqs, p->max_blocks_per_seq,
+							       p->block_size))
+		return fail(ctx, KLLM_ENOSPC);
+	struct kllm_table_args a;
+	memset(&a, 0, sizeof(a));
+	a.tokens = p->token_ids;
+	a.starts = p->token_starts;
+	a.seq_lens = p->seq_lens;
+	a.first_block = p->first_block;
+	a.num_seqs = p->num_seqs;
+	a.max_blocks = p->max_blocks_per_seq;
+	a.block_size = p->block_size;
+	a.index = (uint8_t *)p->index;
+	a.capacity = p->index_capacity;
+	a.now_ns = p->now_ns;
+	a.arena_base = p->arena_base;
+	a.slot_bytes = p->slot_bytes;
+	a.total_slots = p->total_slots;
+	a.k_offset = p->k_offset;
+	a.v_offset = p->v_offset;
+	a.table = p->block_tables;
+	a.hashes = p->hashes;
+	a.midstates = (uint32_t *)p->workspace;
+	a.ms_stride = kllm_table_midstate_stride(p->max_blocks_per_seq, p->block_size);
+	a.miss_list = p->miss_list;
+	a.miss_capacity = p->miss_list ? p->miss_capacity : 0;
+	a.miss_count = p->miss_count;
+	a.hit_miss = (unsigned long long *)p->hit_miss;
+	a.err = p->err_word;
+	int rc = kllm_table_build_launch(&a, pick_stream(ctx, p->stream));
+	if (rc)
+		return cuda_fail(ctx, rc);
+	ctx->stats.launches += 2;
+	return KLLM_OK;
+}
+
 int kllm_gpu_merge_partials(struct kllm_gpu_ctx *ctx, const float *m,
 			    const float *l, const float *o, int num_parts,
 			    int num_rows, int head_dim, void *out, void *stream)

@@ -76,6 +76,18 @@ class PrefillParams(Structure):
                 ("err_word", c_void_p), ("stream", c_void_p)]
 
 
+class TableBuildParams(Structure):
+    _fields_ = [("struct_size", c_uint32), ("flags", c_uint32), ("token_ids", c_void_p),
+                ("token_starts", c_void_p), ("seq_lens", c_void_p), ("first_block", c_void_p),
+                ("num_seqs", c_int), ("max_blocks_per_seq", c_int), ("block_size", c_int),
+                ("index", c_void_p), ("index_capacity", c_uint32), ("now_ns", c_uint64),
+                ("arena_base", c_uint64), ("slot_bytes", c_uint64), ("total_slots", c_uint64),
+                ("k_offset", c_uint64), ("v_offset", c_uint64), ("block_tables", c_void_p),
+                ("hashes", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_uint64),
+                ("miss_list", c_void_p), ("miss_capacity", c_int), ("miss_count", c_void_p),
+                ("hit_miss", c_void_p), ("err_word", c_void_p), ("stream", c_void_p)]
+
+
 class Stats(Structure):
     _fields_ = [("launches", c_uint64), ("kv_bytes", c_uint64), ("errors", c_uint64),
                 ("last_error", c_int), ("device", c_int), ("num_sms", c_int),
@@ -101,6 +113,8 @@ _SIGNATURES = [
     ("kllm_gpu_kv_append_v2", c_int, [c_void_p, POINTER(KvAppendParams)]),
     ("kllm_gpu_gather_debug", c_int, [c_void_p, POINTER(GatherParams)]),
     ("kllm_gpu_prefill_v2", c_int, [c_void_p, POINTER(PrefillParams)]),
+    ("kllm_gpu_table_workspace_size", c_uint64, [c_int, c_int, c_int]),
+    ("kllm_gpu_build_block_tables", c_int, [c_void_p, POINTER(TableBuildParams)]),
     ("kllm_gpu_merge_partials", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("kllm_gpu_memcpy_d2h", c_int, [c_void_p, c_void_p, c_void_p, c_uint64]),
@@ -218,6 +232,13 @@ class Backend:
         for k, v in kw.items():
             setattr(p, k, v)
         return self.lib.kllm_gpu_gather_debug(self.ctx, ctypes.byref(p))
+
+    def build_tables(self, **kw) -> int:
+        p = TableBuildParams()
+        p.struct_size = ctypes.sizeof(TableBuildParams)
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return self.lib.kllm_gpu_build_block_tables(self.ctx, ctypes.byref(p))
 
     def merge(self, m, l, o, num_parts, num_rows, head_dim, out, stream=None) -> int:
         return self.lib.kllm_gpu_merge_partials(self.ctx, m, l, o, num_parts, num_rows,

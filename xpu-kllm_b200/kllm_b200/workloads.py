@@ -149,6 +149,48 @@ C5_SHARED_PREFIX = 1024
 PREFILL_CONFIGS = {C5.name: C5}
 
 
+# Content-addressed block-table builds (token ids -> block keys -> index
+# probe -> table). "warm": every block of every request is in the index (a
+# decode batch whose pages are all resident); "prefix": only the shared
+# prefix chain is (prompt admission with prefix reuse, the rest misses).
+VOCAB = 128256                     # Llama-3 token id range
+
+
+@dataclass(frozen=True)
+class TableConfig:
+    name: str
+    lengths: DecodeConfig          # requests and context lengths
+    warm: str                      # "all" | "prefix"
+    index_capacity: int            # power of two
+
+
+T3 = TableConfig("t3_tables_b256_ctx128-16384_warm", C3, "all", 1 << 17)
+T5 = TableConfig("t5_tables_b16_2048_prefix1024", C5, "prefix", 1 << 12)
+TABLE_CONFIGS = {t.name: t for t in (T3, T5)}
+
+
+def table_tokens(tc: TableConfig, seed: int = 0):
+    """(tokens uint32 packed, starts int64, lens int32): seeded token ids in
+    [0, VOCAB); for the prefix workload the prompts with a cached context
+    share its tokens (so their first blocks have the same keys)."""
+    cfg = tc.lengths
+    rng = np.random.default_rng([seed, 0x7AB1E])
+    if tc.warm == "prefix":
+        ctx, chunk = prefill_split(cfg)
+        lens = (ctx + chunk).astype(np.int32)
+        seqs = [rng.integers(0, VOCAB, int(n)).astype(np.uint32) for n in lens]
+        shared = rng.integers(0, VOCAB, int(ctx.max())).astype(np.uint32)
+        for s in range(len(lens)):
+            if ctx[s]:
+                seqs[s][:ctx[s]] = shared[:ctx[s]]
+    else:
+        lens = context_lengths(cfg, seed).astype(np.int32)
+        seqs = [rng.integers(0, VOCAB, int(n)).astype(np.uint32) for n in lens]
+    tokens = np.concatenate(seqs).astype(np.uint32)
+    starts = np.concatenate([[0], np.cumsum(lens[:-1], dtype=np.int64)]).astype(np.int64)
+    return tokens, starts, lens
+
+
 def prefill_split(cfg: DecodeConfig, shared_prefix: int = C5_SHARED_PREFIX):
     """(cached context, chunk length) per prompt: the first batch/4 prompts
     hit the shared prefix chain."""
