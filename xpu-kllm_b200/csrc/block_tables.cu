@@ -19,7 +19,13 @@
 // prefix ends in message block j. Two kernels:
 //   chain_kernel     one thread per sequence runs the sequential
 //                    compressions over the sequence's full message blocks
-//                    and stores every midstate (32 B) in the workspace;
+//                    and stores every midstate (32 B) in the workspace; its
+//                    tokens arrive through a per-lane shared-memory ring
+//                    (cp.async, three message blocks ahead), so the chain
+//                    never waits on global memory. The chain itself is
+//                    latency-bound: one compression is 64 dependent rounds
+//                    (about 35 cycles each on sm_100: a funnel-shift rotate,
+//                    a three-way xor and a three-way add per critical step);
 //   finalize_kernel  one thread per (sequence, table block): the tail tokens
 //                    and the FIPS 180-4 padding on top of the right midstate
 //                    (one or two compressions), the index probe, the LRU
@@ -115,23 +121,37 @@ __device__ __forceinline__ uint32_t *midstate(const kllm_table_args &a, int s, i
 	return a.midstates + ((size_t)s * a.ms_stride + j) * 8;
 }
 
-__global__ void __launch_bounds__(64) chain_kernel(const kllm_table_args a)
+constexpr int kChainThreads = 64;
+constexpr int kDepth = 4;                       // message blocks in flight per lane
+constexpr int kLaneWords = kDepth * 16 + 4;     // +4: conflict-free 16-byte reads
+
+__device__ __forceinline__ void cp_async4(uint32_t *dst, const uint32_t *src)
 {
+	asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::
+		     "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+
+__global__ void __launch_bounds__(kChainThreads) chain_kernel(const kllm_table_args a)
+{
+	__shared__ __align__(16) uint32_t ring[kChainThreads * kLaneWords];
 	const int s = blockIdx.x * blockDim.x + threadIdx.x;
 	if (s == 0 && a.miss_count)
 		*a.miss_count = 0;
-	if (s >= a.num_seqs)
-		return;
-	const int raw = a.seq_lens[s];
-	if ((long long)raw > (long long)a.max_blocks * a.block_size && a.err)
-		atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
-	const int len = tabled_len(a, s);
-	const int b0 = a.first_block ? max(a.first_block[s], 0) : 0;
-	const int full = len >> 4;                                  // message blocks in the prefix
-	const int j0 = (int)(((long long)b0 * a.block_size) >> 4);  // first one not kept from before
+	int full = 0, j0 = 0;
+	const uint32_t *tok = a.tokens;
+	if (s < a.num_seqs) {
+		const int raw = a.seq_lens[s];
+		if ((long long)raw > (long long)a.max_blocks * a.block_size && a.err)
+			atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
+		const int len = tabled_len(a, s);
+		const int b0 = a.first_block ? max(a.first_block[s], 0) : 0;
+		full = len >> 4;
+		j0 = (int)(((long long)b0 * a.block_size) >> 4);
+		tok = a.tokens + a.starts[s];
+	}
 	if (j0 >= full)
 		return;
-	const uint32_t *tok = a.tokens + a.starts[s];
+	uint32_t *mine = ring + threadIdx.x * kLaneWords;
 	uint32_t h[8];
 	if (j0 == 0) {
 		sha_iv(h);
@@ -141,25 +161,40 @@ __global__ void __launch_bounds__(64) chain_kernel(const kllm_table_args a)
 		h[0] = lo.x; h[1] = lo.y; h[2] = lo.z; h[3] = lo.w;
 		h[4] = hi.x; h[5] = hi.y; h[6] = hi.z; h[7] = hi.w;
 	}
-	uint32_t nxt[16];
 #pragma unroll
-	for (int k = 0; k < 16; ++k)
-		nxt[k] = __ldg(tok + (size_t)j0 * 16 + k);
-	for (int j = j0; j < full; ++j) {
-		uint32_t w[16];
-#pragma unroll
-		for (int k = 0; k < 16; ++k)
-			w[k] = msg_word(nxt[k]);
-		if (j + 1 < full) {           // the next block's tokens load under this compression
+	for (int d = 0; d < kDepth - 1; ++d) {
+		if (j0 + d < full) {
 #pragma unroll
 			for (int k = 0; k < 16; ++k)
-				nxt[k] = __ldg(tok + (size_t)(j + 1) * 16 + k);
+				cp_async4(mine + ((j0 + d) % kDepth) * 16 + k, tok + (size_t)(j0 + d) * 16 + k);
+		}
+		asm volatile("cp.async.commit_group;" ::: "memory");
+	}
+	for (int j = j0; j < full; ++j) {
+		const int jn = j + kDepth - 1;
+		if (jn < full) {
+#pragma unroll
+			for (int k = 0; k < 16; ++k)
+				cp_async4(mine + (jn % kDepth) * 16 + k, tok + (size_t)jn * 16 + k);
+		}
+		asm volatile("cp.async.commit_group;" ::: "memory");
+		asm volatile("cp.async.wait_group %0;" :: "n"(kDepth - 1) : "memory");
+		const uint4 *src = reinterpret_cast<const uint4 *>(mine + (j % kDepth) * 16);
+		uint32_t w[16];
+#pragma unroll
+		for (int q = 0; q < 4; ++q) {
+			const uint4 v = src[q];
+			w[4 * q] = msg_word(v.x);
+			w[4 * q + 1] = msg_word(v.y);
+			w[4 * q + 2] = msg_word(v.z);
+			w[4 * q + 3] = msg_word(v.w);
 		}
 		sha_compress(h, w);
 		uint4 *m = reinterpret_cast<uint4 *>(midstate(a, s, j + 1));
 		m[0] = make_uint4(h[0], h[1], h[2], h[3]);
 		m[1] = make_uint4(h[4], h[5], h[6], h[7]);
 	}
+	asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(256) finalize_kernel(const kllm_table_args a)
@@ -301,7 +336,7 @@ extern "C" uint64_t kllm_table_midstate_stride(int max_blocks, int block_size)
 extern "C" int kllm_table_build_launch(const struct kllm_table_args *a, void *stream)
 {
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
-	const int chain_threads = 64;
+	const int chain_threads = kChainThreads;
 	chain_kernel<<<(a->num_seqs + chain_threads - 1) / chain_threads, chain_threads, 0, st>>>(*a);
 	cudaError_t e = cudaGetLastError();
 	if (e != cudaSuccess)
