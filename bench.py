@@ -399,6 +399,9 @@ def run_kllm(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_from_rig(rig, args)
+    per_req = None
+    if args.per_request_compare and world == 1 and not split_kv:
+        per_req = per_request_step_ms(rig, torch, max(1, min(args.steps, 3)))
 
     if world > 1:
         dist.barrier()
@@ -447,12 +450,53 @@ def run_kllm(args) -> None:
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if per_req is not None:
+            line["per_request_launches"] = {
+                "ms_per_step": round(per_req[0], 3), "launches_per_step": per_req[1],
+                "batched_ms_per_step": round(ms_step, 4),
+                "note": "the same step with one decode launch per request per layer, the "
+                        "pattern of userspace/reactor/batch_scheduler.c:258-263"}
         print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
     torch.cuda.set_stream(torch.cuda.default_stream())
     be.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def per_request_step_ms(rig, torch, steps: int):
+    """(ms per step, launches per step) of the step issued one request at a
+    time: every layer, every request gets its own decode launch (table row,
+    seq_len, query and output rows of that request)."""
+    c = rig.cfg
+    st = torch.cuda.current_stream()
+    sp = st.cuda_stream
+    row_b = rig.plan.max_blocks * 24
+    q_b = c.hq * c.d * 2
+
+    def one_step():
+        for layer in range(c.layers):
+            for s in range(rig.B):
+                rc = rig.be.decode_v2(
+                    output=rig.out[layer].data_ptr() + s * q_b,
+                    query=rig.q[layer].data_ptr() + s * q_b,
+                    block_tables=rig.table.data_ptr() + s * row_b,
+                    seq_lens=rig.seq_lens.data_ptr() + 4 * s, num_seqs=1, num_heads=c.hq,
+                    num_kv_heads=c.hkv, head_dim=c.d, max_blocks_per_seq=rig.plan.max_blocks,
+                    block_size=c.block, kv_dtype=c.kv_dtype, layer=layer,
+                    layer_stride=rig.layer_stride, scale=c.scale, split=1, stream=sp)
+                if rc != 0:
+                    raise RuntimeError(f"decode launch failed: {rc}")
+    one_step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        one_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, c.layers * rig.B
 
 
 def cpu_baseline_from_rig(rig, args) -> dict:
@@ -1167,6 +1211,9 @@ def main():
                     choices=["layer-major", "slot-major"],
                     help="layer-major: each layer's pages form one region (layer_stride = "
                          "n_slots x 2 pages); slot-major: a slot holds all layers of a block")
+    ap.add_argument("--per-request-compare", action="store_true",
+                    help="also time the decode step issued one request per launch (the "
+                         "reference scheduler's loop), reported beside the batched step")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (smaller captures for profiling)")
     args = ap.parse_args()
