@@ -1139,6 +1139,105 @@ def run_reference_tables(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+ARRIVAL_METRIC = "KV block arrival into VRAM by content key (wavefront submit -> poll): GB/s"
+
+
+def run_arrival(args) -> None:
+    """Store file of random block records in a temporary directory (page
+    cache resident: this measures the host-staged path, not a drive), an
+    index of their keys, then per step 64 wavefronts of 64 blocks each
+    submitted and polled to completion; wall time on the host from the first
+    submit to the last completion (the completions are observed by polling)."""
+    import ctypes
+    import tempfile
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(local)
+    import kllm_b200 as kb
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import tablecase as tc
+    acfg = wl.ARRIVAL_CONFIGS[args.config]
+    lib = kb.load()
+    rng = np.random.default_rng(args.seed)
+    n, rb = acfg.blocks, acfg.record_bytes
+    data = rng.integers(0, 256, (n, rb), dtype=np.uint8)
+    keys = [rng.integers(0, 256, 32, dtype=np.uint8).tobytes() for _ in range(n)]
+    entries = tc.empty_index(1 << (2 * n - 1).bit_length())
+    for r in range(n):
+        tc.index_insert(entries, keys[r], r)
+    dev = torch.zeros(n * rb, dtype=torch.uint8, device=f"cuda:{local}")
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "kv_store.bin")
+        with open(path, "wb") as f:
+            f.write(data.tobytes())
+        ctx = lib.kllm_wavefront_create2(path.encode(), local, rb, acfg.staging)
+        if not ctx:
+            raise RuntimeError("kllm_wavefront_create2 failed")
+        try:
+            assert lib.kllm_wavefront_set_index(ctx, entries.ctypes.data, len(entries), rb,
+                                                0) == 0
+            perm = rng.permutation(n)
+            wfs = []
+            for w in range(0, n, 64):
+                wf = kb.Wavefront()
+                wf.num_blocks, wf.flags, wf.sequence_id = 64, 2, w
+                for i in range(64):
+                    r = int(perm[w + i])
+                    ctypes.memmove(wf.blocks[i].obj_key, keys[r], 32)
+                    wf.blocks[i].vram_dest_addr = dev.data_ptr() + (w + i) * rb
+                    wf.blocks[i].block_size = rb
+                wfs.append(wf)
+            comp = (kb.WfCompletion * 64)()
+
+            def one_step():
+                for wf in wfs:
+                    if lib.kllm_wavefront_submit(ctx, ctypes.byref(wf)) != 0:
+                        raise RuntimeError("kllm_wavefront_submit refused")
+                done = failed = 0
+                while done < len(wfs):
+                    k = lib.kllm_wavefront_wait(ctx, comp, 64, 10000)
+                    if k <= 0:
+                        raise RuntimeError("no wavefront completion within 10 s")
+                    done += k
+                    failed += sum(comp[i].blocks_failed for i in range(k))
+                return failed
+
+            for _ in range(args.warmup):
+                assert one_step() == 0
+            torch.cuda.synchronize()
+            host = dev.cpu().numpy().reshape(n, rb)
+            assert np.array_equal(host, data[perm]), "arrived blocks differ from the store"
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                one_step()
+            t = time.perf_counter() - t0
+            assert lib.kllm_wavefront_error(ctx) == 0
+        finally:
+            lib.kllm_wavefront_destroy(ctx)
+    if rank == 0:
+        gbs = n * rb * args.steps / t / 1e9
+        line = {
+            "metric": ARRIVAL_METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded random block records in a page-cached store file)",
+            "config": {"workload": acfg.name, "blocks": n, "record_bytes": rb,
+                       "wavefronts_per_step": n // 64, "staging_buffers": acfg.staging,
+                       "source": "page cache (host-staged path; no NVMe drive measured)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 3), "peak": peaks()[0],
+                         "unit": "GB/s", "frac": round(gbs / peaks()[0], 5),
+                         "peak_kind": peaks()[1], "traffic": None,
+                         "note": "host-side path: pread into page-locked staging and "
+                                 "host-to-device copies; HBM is not the bound"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": n * rb,
+                    "d2h_bytes_per_step": 0},
+            "gpu_launches": 0,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1200,7 +1299,7 @@ def main():
     ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
     ap.add_argument("--config", default=wl.C3.name,
                     choices=list(wl.CONFIGS) + list(wl.PREFILL_CONFIGS) +
-                    list(wl.TABLE_CONFIGS))
+                    list(wl.TABLE_CONFIGS) + list(wl.ARRIVAL_CONFIGS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1222,6 +1321,16 @@ def main():
     prefill = args.config in wl.PREFILL_CONFIGS
     if args.config in wl.TABLE_CONFIGS:
         (run_reference_tables if args.impl == "reference" else run_tables)(args)
+        return
+    if args.config in wl.ARRIVAL_CONFIGS:
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference's kllm_wavefront_submit/poll are stubs "
+                                  "(userspace/gpu/nvme_ep_wavefront.c:74-104): nothing is "
+                                  "read and no completion is ever reported"}), flush=True)
+            return
+        run_arrival(args)
         return
     if args.impl == "reference":
         (run_reference_prefill if prefill else run_reference)(args)

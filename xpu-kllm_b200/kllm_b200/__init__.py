@@ -88,6 +88,27 @@ class TableBuildParams(Structure):
                 ("hit_miss", c_void_p), ("err_word", c_void_p), ("stream", c_void_p)]
 
 
+class WfBlockDesc(Structure):
+    """userspace/gpu/nvme_ep_wavefront.h:32-39"""
+    _fields_ = [("obj_key", c_uint8 * 32), ("vram_dest_addr", c_uint64), ("block_size", c_uint32),
+                ("layer_start", c_uint32), ("layer_count", c_uint32), ("_pad", c_uint32)]
+
+
+WAVEFRONT_MAX_BLOCKS = 64
+
+
+class Wavefront(Structure):
+    """userspace/gpu/nvme_ep_wavefront.h:42-47"""
+    _fields_ = [("num_blocks", c_uint32), ("flags", c_uint32), ("sequence_id", c_uint64),
+                ("blocks", WfBlockDesc * WAVEFRONT_MAX_BLOCKS)]
+
+
+class WfCompletion(Structure):
+    """userspace/gpu/nvme_ep_wavefront.h:54-60"""
+    _fields_ = [("sequence_id", c_uint64), ("blocks_completed", c_uint32),
+                ("blocks_failed", c_uint32), ("total_bytes", c_uint64), ("latency_ns", c_uint64)]
+
+
 class Stats(Structure):
     _fields_ = [("launches", c_uint64), ("kv_bytes", c_uint64), ("errors", c_uint64),
                 ("last_error", c_int), ("device", c_int), ("num_sms", c_int),
@@ -136,6 +157,19 @@ _SIGNATURES = [
     ("kllm_gpu_p2p_destroy", None, [c_void_p]),
 ]
 
+# every symbol include/kllm_wavefront.h declares
+_WF_SIGNATURES = [
+    ("kllm_wavefront_create", c_void_p, [ctypes.c_char_p]),
+    ("kllm_wavefront_create2", c_void_p, [ctypes.c_char_p, c_int, c_uint64, c_int]),
+    ("kllm_wavefront_destroy", None, [c_void_p]),
+    ("kllm_wavefront_set_index", c_int, [c_void_p, c_void_p, c_uint32, c_uint64, c_uint64]),
+    ("kllm_wavefront_submit", c_int, [c_void_p, POINTER(Wavefront)]),
+    ("kllm_wavefront_poll", c_int, [c_void_p, POINTER(WfCompletion), c_int]),
+    ("kllm_wavefront_wait", c_int, [c_void_p, POINTER(WfCompletion), c_int, c_int]),
+    ("kllm_wavefront_error", c_int, [c_void_p]),
+]
+WAVEFRONT_HEADER_PATH = os.path.join(os.path.dirname(HEADER_PATH), "kllm_wavefront.h")
+
 _LIB = None
 
 
@@ -148,7 +182,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
     if not os.path.exists(p):
         raise RuntimeError(f"libkllm_gpu.so not built: {p} (run __graft_entry__.build())")
     lib = ctypes.CDLL(p)
-    for name, res, args in _SIGNATURES:
+    for name, res, args in _SIGNATURES + _WF_SIGNATURES:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
@@ -159,6 +193,10 @@ def load(path: str | None = None) -> ctypes.CDLL:
 
 def symbols() -> list[str]:
     return [s[0] for s in _SIGNATURES]
+
+
+def wavefront_symbols() -> list[str]:
+    return [s[0] for s in _WF_SIGNATURES]
 
 
 class Backend:

@@ -169,6 +169,22 @@ T5 = TableConfig("t5_tables_b16_2048_prefix1024", C5, "prefix", 1 << 12)
 TABLE_CONFIGS = {t.name: t for t in (T3, T5)}
 
 
+# KV block arrival into VRAM (the wavefront path): `blocks` records of
+# `record_bytes` (one 16-token MX-FP8 K+V page pair of one layer: 2 x 8 kv
+# heads x (16 x 128 + 16 x 16) bytes) fetched by key from a store file, in
+# wavefronts of 64 blocks.
+@dataclass(frozen=True)
+class ArrivalConfig:
+    name: str
+    blocks: int
+    record_bytes: int
+    staging: int                   # page-locked staging buffers
+
+
+W3 = ArrivalConfig("w3_kv_arrival_4096x36k", 4096, 36864, 8)
+ARRIVAL_CONFIGS = {W3.name: W3}
+
+
 def table_tokens(tc: TableConfig, seed: int = 0):
     """(tokens uint32 packed, starts int64, lens int32): seeded token ids in
     [0, VOCAB); for the prefix workload the prompts with a cached context
