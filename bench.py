@@ -1139,6 +1139,166 @@ def run_reference_tables(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+LM_HEAD_METRIC = "lm_head projection + token sampling: tokens/s (rows sampled per second)"
+
+
+def run_lm_head(args) -> None:
+    import torch
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ["KLLM_GPU_DEVICE"] = str(local)
+    import kllm_b200 as kb
+    be = kb.Backend()
+    if be.backend != kb.KLLM_GPU_CUDA:
+        raise RuntimeError("libkllm_gpu: no sm_100 device")
+    torch.cuda.set_stream(be.torch_stream())
+    c = wl.LM_HEAD_CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed * 1000003 + 41)
+    R, H, V = c.rows, c.hidden, c.vocab
+    hid = torch.randn((R, H), generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn((V, H), generator=g, device=dev) * (1.5 / math.sqrt(H))).to(torch.bfloat16)
+    logits = torch.empty((R, V), dtype=torch.float32, device=dev)
+    tok = torch.empty(R, dtype=torch.int32, device=dev)
+    ws_b = be.lib.kllm_gpu_lm_head_workspace_size(R, V)
+    ws = torch.empty(ws_b, dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    rng = np.random.default_rng(args.seed)
+    if c.sampling == "greedy":
+        meth = temp = topk = None
+    else:
+        meth = torch.from_numpy(rng.choice([0, 1, 2, 3], R).astype(np.int32)).to(dev)
+        temp = torch.from_numpy(rng.choice([0.7, 1.0], R).astype(np.float32)).to(dev)
+        topk = torch.from_numpy(rng.choice([40, 50, 200], R).astype(np.int32)).to(dev)
+    uni = torch.from_numpy(rng.random(R).astype(np.float32)).to(dev)
+    st = torch.cuda.current_stream()
+    sp = st.cuda_stream
+
+    def step(hptr=None):
+        rc = be.lm_head(hidden=hptr or hid.data_ptr(), weight=w.data_ptr(), num_rows=R,
+                        hidden_dim=H, vocab=V, logits=logits.data_ptr(),
+                        method=meth.data_ptr() if meth is not None else None,
+                        temperature=temp.data_ptr() if temp is not None else None,
+                        top_k=topk.data_ptr() if topk is not None else None,
+                        uniform=uni.data_ptr(), tokens=tok.data_ptr(), workspace=ws.data_ptr(),
+                        workspace_bytes=ws_b, err_word=err.data_ptr(), stream=sp)
+        if rc != 0:
+            raise RuntimeError(f"lm_head failed: {rc}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # a spot check of the tokens against the logits the kernel wrote
+    lg0 = logits[0].cpu().numpy()
+    if c.sampling == "greedy":
+        assert int(tok[0].item()) == int(np.argmax(lg0)), "greedy token is not the argmax"
+    assert int(err.item()) == 0
+    clk = Clocks(local)
+    clk.start()
+    launches0 = be.stats().launches
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        step()          # weights 1.05 GB per step: every step streams past the 126 MB L2
+    e1.record(st)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = be.stats().launches - launches0
+    t_ms = e0.elapsed_time(e1)
+    # end to end through the C ABI: pinned hidden states in, tokens out
+    h_h = hid.cpu().pin_memory()
+    h_t = torch.empty(R, dtype=torch.int32).pin_memory()
+    d_h = torch.empty_like(hid)
+    lib, ctx = be.lib, be.ctx
+
+    def e2e_step():
+        lib.kllm_gpu_memcpy_h2d_async(ctx, d_h.data_ptr(), h_h.data_ptr(), R * H * 2, sp)
+        step(d_h.data_ptr())
+        lib.kllm_gpu_memcpy_d2h_async(ctx, h_t.data_ptr(), tok.data_ptr(), R * 4, sp)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    te_ms = e0.elapsed_time(e1)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = lm_head_cpu_sample(hid, w, R, V, args.cpu_seconds)
+    if rank == 0:
+        per = t_ms / args.steps
+        flops = 2.0 * R * H * V
+        nbytes = V * H * 2 + R * H * 2 + R * V * 4
+        hpeak, hkind = peaks()
+        tpeak, tkind = bf16_peak()
+        gbs = nbytes / (per * 1e-3) / 1e9
+        line = {
+            "metric": LM_HEAD_METRIC, "value": round(R * args.steps / (t_ms * 1e-3), 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded torch.randn hidden states and weights)",
+            "config": {"workload": c.name, "rows": R, "hidden": H, "vocab": V,
+                       "sampling": c.sampling,
+                       "l2": "weights 1.05 GB per step, larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hpeak, "unit": "GB/s",
+                         "frac": round(gbs / hpeak, 4), "peak_kind": hkind, "traffic": None,
+                         "kernel": "lm_head_kernel<2> + sample_kernel (one step)",
+                         "algorithmic_bytes": nbytes},
+            "tensor": {"achieved_tflops": round(flops / (per * 1e-3) / 1e12, 1),
+                       "peak": tpeak, "frac": round(flops / (per * 1e-3) / 1e12 / tpeak, 4)},
+            "e2e": {"value": round(R * args.steps / (te_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": R * H * 2, "d2h_bytes_per_step": R * 4},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream())
+    be.close()
+
+
+def lm_head_cpu_sample(hid, w, R, V, seconds):
+    """The projection of one row against the whole vocabulary by the oracle
+    port (the reference has no lm_head: its GPU path returns zero logits),
+    then the reference's own greedy sampler (decode_loop.c:58-70) over those
+    logits, scaled to the batch."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    h = hid[:1].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+    wt = w.contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    lg = oracle.lm_head_logits(h, wt)[0]
+    t_proj = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    if oracle.ref_sampling_lib() is not None:
+        oracle.ref_sampling_lib().ref_sample_token(oracle.ptr(lg), V, 0, 0.0, 0, 0.0)
+        kind = "port (projection) + reference (sampler)"
+    else:
+        oracle.sample_token(lg, 0, 0.0, 0, 0.0)
+        kind = "port"
+    t_samp = time.perf_counter() - t0
+    per_row = t_proj + t_samp
+    return {"value": round(1.0 / per_row, 3), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "detail": kind, "projection_s_per_row": round(t_proj, 4),
+            "sampling_s_per_row": round(t_samp, 6),
+            "sample": f"one row x {V} vocabulary rows x {hid.shape[1]} (fp32 sums), then "
+                      "greedy sampling; per row, so tokens/s for the batch is the same"}
+
+
+def torch_int16():
+    import torch
+    return torch.int16
+
+
 ARRIVAL_METRIC = "KV block arrival into VRAM by content key (wavefront submit -> poll): GB/s"
 
 
@@ -1299,7 +1459,8 @@ def main():
     ap.add_argument("--impl", default="kllm", choices=["kllm", "reference"])
     ap.add_argument("--config", default=wl.C3.name,
                     choices=list(wl.CONFIGS) + list(wl.PREFILL_CONFIGS) +
-                    list(wl.TABLE_CONFIGS) + list(wl.ARRIVAL_CONFIGS))
+                    list(wl.TABLE_CONFIGS) + list(wl.ARRIVAL_CONFIGS) +
+                    list(wl.LM_HEAD_CONFIGS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1321,6 +1482,16 @@ def main():
     prefill = args.config in wl.PREFILL_CONFIGS
     if args.config in wl.TABLE_CONFIGS:
         (run_reference_tables if args.impl == "reference" else run_tables)(args)
+        return
+    if args.config in wl.LM_HEAD_CONFIGS:
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference has no lm_head: its GPU inference returns an "
+                                  "all-zero logit vector and takes its argmax "
+                                  "(userspace/compute/infer_gpu.c:212-229)"}), flush=True)
+            return
+        run_lm_head(args)
         return
     if args.config in wl.ARRIVAL_CONFIGS:
         if args.impl == "reference":

@@ -133,6 +133,7 @@ int kllm_gpu_paged_attention_cuda(
 #define KLLM_ERR_MISALIGNED     0x2u  /* page pointer not 16-byte aligned: page skipped */
 #define KLLM_ERR_APPEND_NOPAGE  0x4u  /* append target page invalid / position out of table */
 #define KLLM_ERR_TIMEOUT        0x8u  /* a bounded device-side wait expired; the warp stopped */
+#define KLLM_ERR_TOPK_RANGE     0x10u /* lm_head: top_k in (1024, vocab): token -1 for that row */
 
 /* KV page formats. One page holds `block_size` tokens of one layer.
  *
@@ -441,6 +442,56 @@ uint64_t kllm_gpu_table_workspace_size(int num_seqs, int max_blocks_per_seq,
 				       int block_size);
 int kllm_gpu_build_block_tables(struct kllm_gpu_ctx *ctx,
 				const struct kllm_gpu_table_build_params *p);
+
+/* Vocabulary projection (lm_head) and token sampling on the GPU: the step
+ * after attention. The reference's GPU inference returns zero logits and
+ * takes their argmax (userspace/compute/infer_gpu.c:212-229); its samplers
+ * are host loops (userspace/decode/decode_loop.c:58-185), restated here:
+ *   logits[r][v] = sum_k hidden[r][k] * weight[v][k]   (bf16 in, fp32 sums,
+ *                                                       tcgen05 tensor cores)
+ *   method GREEDY      first maximum logit
+ *          TEMPERATURE first index whose running sum of exp((l - max) / T)
+ *                      reaches uniform[r] x the total (T <= 0: greedy)
+ *          TOP_K       the top_k[r] largest logits in (value desc, index asc)
+ *                      order, then the temperature draw over them (top_k 0 or
+ *                      >= vocab: TEMPERATURE; at most 1024)
+ *          TOP_P       as TEMPERATURE (the reference's nucleus is a TODO)
+ * uniform[r] in [0, 1] stands for the reference's rand() / RAND_MAX. The
+ * full-vocabulary temperature sum runs in parallel, so where r lands within
+ * rounding of a cumulative boundary the token can be the neighbour of the
+ * one a sequential sum picks. num_rows <= 256, hidden_dim % 64 == 0,
+ * hidden and weight 16-byte aligned. logits is required unless every row
+ * is greedy (method NULL). */
+enum kllm_sampling {                    /* userspace/decode/decode_loop.h:27-32 */
+	KLLM_SAMPLE_GREEDY = 0,
+	KLLM_SAMPLE_TOP_K = 1,
+	KLLM_SAMPLE_TOP_P = 2,
+	KLLM_SAMPLE_TEMPERATURE = 3,
+};
+
+struct kllm_gpu_lm_head_params {
+	uint32_t struct_size;
+	uint32_t flags;
+	const void *hidden;          /* bf16 [num_rows][hidden_dim] */
+	const void *weight;          /* bf16 [vocab][hidden_dim] */
+	int num_rows;
+	int hidden_dim;
+	int vocab;
+	float *logits;               /* out: fp32 [num_rows][vocab], or NULL (greedy only) */
+	const int *method;           /* [num_rows] enum kllm_sampling, or NULL (all greedy) */
+	const float *temperature;    /* [num_rows], or NULL */
+	const int *top_k;            /* [num_rows], or NULL */
+	const float *uniform;        /* [num_rows] in [0, 1], or NULL */
+	int *tokens;                 /* out: [num_rows] */
+	void *workspace;             /* kllm_gpu_lm_head_workspace_size bytes, 16-byte aligned */
+	uint64_t workspace_bytes;
+	uint32_t *err_word;
+	void *stream;
+};
+
+uint64_t kllm_gpu_lm_head_workspace_size(int num_rows, int vocab);
+int kllm_gpu_lm_head_sample(struct kllm_gpu_ctx *ctx,
+			    const struct kllm_gpu_lm_head_params *p);
 
 /* Cross-GPU split-KV exchange over peer memory (no counterpart in the
  * reference): the same result as kllm_gpu_comm_merge, computed by one kernel

@@ -153,6 +153,20 @@ int orc_build_block_tables(const uint32_t *tokens, const int64_t *starts,
 			   struct orc_entry *table, uint8_t *hashes,
 			   uint64_t *hits, uint64_t *misses);
 
+/* ---- vocabulary projection and sampling (sampling.c) --------------------- */
+
+/* logits[r][j] = sum_k hidden[r][k] * weight[v_j][k] (fp32, k ascending) for
+ * the vocabulary rows v_j = vocab_ids[j] (all rows 0..n_ids-1 when NULL). */
+void orc_lm_head_logits(const uint16_t *hidden, const uint16_t *weight, int rows, int hidden_dim,
+			int vocab, const int32_t *vocab_ids, int n_ids, float *out);
+/* decode_loop.c:58-183 with the uniform draw r given */
+uint32_t orc_sample_greedy(const float *logits, uint32_t vocab);
+uint32_t orc_sample_temperature(const float *logits, uint32_t vocab, float temperature, float r);
+uint32_t orc_sample_top_k(const float *logits, uint32_t vocab, uint32_t k, float temperature,
+			  float r);
+uint32_t orc_sample_token(const float *logits, uint32_t vocab, int method, float temperature,
+			  uint32_t top_k, float r);
+
 #ifdef __cplusplus
 }
 #endif

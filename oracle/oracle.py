@@ -86,6 +86,17 @@ def _bind(lib, prefix):
                                            c_int, c_void_p, c_uint32, c_uint64, c_uint64,
                                            c_uint64, c_uint64, c_uint64, c_uint64, c_void_p,
                                            c_void_p, POINTER(c_uint64), POINTER(c_uint64)]
+    lib.orc_lm_head_logits.restype = None
+    lib.orc_lm_head_logits.argtypes = [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int,
+                                       c_void_p]
+    lib.orc_sample_greedy.restype = c_uint32
+    lib.orc_sample_greedy.argtypes = [c_void_p, c_uint32]
+    lib.orc_sample_temperature.restype = c_uint32
+    lib.orc_sample_temperature.argtypes = [c_void_p, c_uint32, c_float, c_float]
+    lib.orc_sample_top_k.restype = c_uint32
+    lib.orc_sample_top_k.argtypes = [c_void_p, c_uint32, c_uint32, c_float, c_float]
+    lib.orc_sample_token.restype = c_uint32
+    lib.orc_sample_token.argtypes = [c_void_p, c_uint32, c_int, c_float, c_uint32, c_float]
     h = getattr(lib, f"{prefix}_harness_paged_decode")
     h.restype = c_int
     h.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
@@ -149,6 +160,42 @@ def ref():
 
 
 _REF_INDEX = None
+_REF_SAMPLING = None
+
+
+def ref_sampling_lib():
+    """The reference's own samplers (decode_loop.c), None when never built."""
+    global _REF_SAMPLING
+    if _REF_SAMPLING is None:
+        p = os.path.join(REF_DIR, "libkllm_ref_sampling.so")
+        if not os.path.exists(p):
+            return None
+        lib = ctypes.CDLL(p)
+        lib.ref_sample_token.restype = c_uint32
+        lib.ref_sample_token.argtypes = [c_void_p, c_uint32, c_int, c_float, c_uint32, c_float]
+        lib.ref_srand.restype = None
+        lib.ref_srand.argtypes = [ctypes.c_uint]
+        lib.ref_rand.restype = c_int
+        lib.ref_rand.argtypes = []
+        _REF_SAMPLING = lib
+    return _REF_SAMPLING
+
+
+RAND_MAX = 2147483647
+
+
+def ref_sample_with_seed(logits, method, temperature, top_k, seed):
+    """The reference's sample_token with its rand() seeded; returns (token,
+    r) where r is the draw the reference makes, as float32 like its
+    (float)rand() / (float)RAND_MAX (decode_loop.c:95)."""
+    lib = ref_sampling_lib()
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    lib.ref_srand(seed)
+    x = lib.ref_rand()
+    r = np.float32(np.float32(x) / np.float32(RAND_MAX))
+    lib.ref_srand(seed)
+    tok = lib.ref_sample_token(ptr(lg), len(lg), method, temperature, top_k, 0.0)
+    return int(tok), float(r)
 
 
 def ref_index_lib():
@@ -423,3 +470,24 @@ class RefIndex:
                                          block_size, ptr(slots), ptr(keys), nthreads, t)
         assert rc == 0
         return slots, keys, t[0], t[1]
+
+
+# ---- vocabulary projection and sampling ---------------------------------------
+
+def lm_head_logits(hidden, weight, vocab_ids=None):
+    """fp32 logits [rows][len(vocab_ids) or vocab] of bf16 hidden x weight^T."""
+    h = np.ascontiguousarray(hidden, dtype=np.uint16)
+    w = np.ascontiguousarray(weight, dtype=np.uint16)
+    rows, hd = h.shape
+    vocab = w.shape[0]
+    ids = None if vocab_ids is None else np.ascontiguousarray(vocab_ids, dtype=np.int32)
+    n = vocab if ids is None else len(ids)
+    out = np.zeros((rows, n), dtype=np.float32)
+    orc().orc_lm_head_logits(ptr(h), ptr(w), rows, hd, vocab, None if ids is None else ptr(ids),
+                             n, ptr(out))
+    return out
+
+
+def sample_token(logits, method, temperature, top_k, r):
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(orc().orc_sample_token(ptr(lg), len(lg), method, temperature, top_k, r))

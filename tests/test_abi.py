@@ -54,6 +54,7 @@ STRUCTS = {
     "kllm_gpu_gather_params": kb.GatherParams,
     "kllm_gpu_prefill_params": kb.PrefillParams,
     "kllm_gpu_table_build_params": kb.TableBuildParams,
+    "kllm_gpu_lm_head_params": kb.LmHeadParams,
     "kllm_gpu_stats": kb.Stats,
 }
 

@@ -20,6 +20,7 @@ extern "C" {
 
 #define KLLM_ERR_SEQ_TOO_LONG_BIT 0x1u /* seq_len beyond the table: clamped */
 #define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
+#define KLLM_ERR_TOPK_RANGE_BIT 0x10u /* a row asked for top-k above 1024 */
 /* MX-FP8 decode computes with K/V values scaled by 2^-2 (payload x scale
  * stays below the f16 maximum); scores and outputs are multiplied back. */
 #define KLLM_MX_DEC_UNBIAS   4.0f
@@ -157,6 +158,29 @@ struct kllm_table_args {
 };
 uint64_t kllm_table_midstate_stride(int max_blocks, int block_size);
 int kllm_table_build_launch(const struct kllm_table_args *a, void *stream);
+
+/* Vocabulary projection + sampling (lm_head.cu). Sampling methods as
+ * userspace/decode/decode_loop.h:27-32 numbers them. */
+#define KLLM_SAMPLE_GREEDY_I      0
+#define KLLM_SAMPLE_TOP_K_I       1
+#define KLLM_SAMPLE_TOP_P_I       2
+#define KLLM_SAMPLE_TEMPERATURE_I 3
+struct kllm_lm_head_args {
+	const void *hidden;       /* bf16 [num_rows][hidden_dim] */
+	const void *weight;       /* bf16 [vocab][hidden_dim] */
+	int num_rows, hidden_dim, vocab;
+	float *logits;            /* fp32 [num_rows][vocab] or NULL */
+	const int *method;        /* [num_rows] or NULL (greedy) */
+	const float *temperature; /* [num_rows] or NULL */
+	const int *top_k;         /* [num_rows] or NULL */
+	const float *uniform;     /* [num_rows] or NULL */
+	int *tokens;              /* [num_rows] */
+	float *part_m, *part_s;   /* [num_rows][tiles] */
+	int *part_a;              /* [num_rows][tiles] */
+	uint32_t *err;
+};
+int kllm_lm_head_tiles(int vocab);
+int kllm_lm_head_launch(const struct kllm_lm_head_args *a, void *stream);
 
 #ifdef __cplusplus
 }

@@ -846,6 +846,53 @@ int kllm_gpu_build_block_tables(struct kllm_gpu_ctx *ctx,
 	return KLLM_OK;
 }
 
+uint64_t kllm_gpu_lm_head_workspace_size(int num_rows, int vocab)
+{
+	if (num_rows <= 0 || vocab <= 0)
+		return 0;
+	return (uint64_t)num_rows * (uint64_t)kllm_lm_head_tiles(vocab) * 12u + 32u;
+}
+
+int kllm_gpu_lm_head_sample(struct kllm_gpu_ctx *ctx, const struct kllm_gpu_lm_head_params *p)
+{
+	if (!p || p->struct_size < sizeof(*p))
+		return fail(ctx, KLLM_EINVAL);
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (p->num_rows <= 0 || p->hidden_dim <= 0 || p->vocab <= 0 || !p->hidden || !p->weight ||
+	    !p->tokens || !p->workspace || (p->method && !p->logits))
+		return fail(ctx, KLLM_EINVAL);
+	if (p->num_rows > 256 || p->hidden_dim % 64)
+		return fail(ctx, KLLM_ENOSYS);
+	if (((uintptr_t)p->hidden | (uintptr_t)p->weight | (uintptr_t)p->workspace) & 15u)
+		return fail(ctx, KLLM_EINVAL);
+	if (p->workspace_bytes < kllm_gpu_lm_head_workspace_size(p->num_rows, p->vocab))
+		return fail(ctx, KLLM_ENOSPC);
+	const uint64_t tiles = (uint64_t)kllm_lm_head_tiles(p->vocab) * (uint64_t)p->num_rows;
+	struct kllm_lm_head_args a;
+	memset(&a, 0, sizeof(a));
+	a.hidden = p->hidden;
+	a.weight = p->weight;
+	a.num_rows = p->num_rows;
+	a.hidden_dim = p->hidden_dim;
+	a.vocab = p->vocab;
+	a.logits = p->logits;
+	a.method = p->method;
+	a.temperature = p->temperature;
+	a.top_k = p->top_k;
+	a.uniform = p->uniform;
+	a.tokens = p->tokens;
+	a.part_m = (float *)p->workspace;
+	a.part_s = a.part_m + tiles;
+	a.part_a = (int *)(a.part_s + tiles);
+	a.err = p->err_word;
+	int rc = kllm_lm_head_launch(&a, pick_stream(ctx, p->stream));
+	if (rc)
+		return cuda_fail(ctx, rc);
+	ctx->stats.launches += 2;
+	return KLLM_OK;
+}
+
 int kllm_gpu_merge_partials(struct kllm_gpu_ctx *ctx, const float *m,
 			    const float *l, const float *o, int num_parts,
 			    int num_rows, int head_dim, void *out, void *stream)

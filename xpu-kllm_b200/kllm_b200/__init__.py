@@ -88,6 +88,18 @@ class TableBuildParams(Structure):
                 ("hit_miss", c_void_p), ("err_word", c_void_p), ("stream", c_void_p)]
 
 
+class LmHeadParams(Structure):
+    _fields_ = [("struct_size", c_uint32), ("flags", c_uint32), ("hidden", c_void_p),
+                ("weight", c_void_p), ("num_rows", c_int), ("hidden_dim", c_int), ("vocab", c_int),
+                ("logits", c_void_p), ("method", c_void_p), ("temperature", c_void_p),
+                ("top_k", c_void_p), ("uniform", c_void_p), ("tokens", c_void_p),
+                ("workspace", c_void_p), ("workspace_bytes", c_uint64), ("err_word", c_void_p),
+                ("stream", c_void_p)]
+
+
+SAMPLE_GREEDY, SAMPLE_TOP_K, SAMPLE_TOP_P, SAMPLE_TEMPERATURE = 0, 1, 2, 3
+
+
 class WfBlockDesc(Structure):
     """userspace/gpu/nvme_ep_wavefront.h:32-39"""
     _fields_ = [("obj_key", c_uint8 * 32), ("vram_dest_addr", c_uint64), ("block_size", c_uint32),
@@ -136,6 +148,8 @@ _SIGNATURES = [
     ("kllm_gpu_prefill_v2", c_int, [c_void_p, POINTER(PrefillParams)]),
     ("kllm_gpu_table_workspace_size", c_uint64, [c_int, c_int, c_int]),
     ("kllm_gpu_build_block_tables", c_int, [c_void_p, POINTER(TableBuildParams)]),
+    ("kllm_gpu_lm_head_workspace_size", c_uint64, [c_int, c_int]),
+    ("kllm_gpu_lm_head_sample", c_int, [c_void_p, POINTER(LmHeadParams)]),
     ("kllm_gpu_merge_partials", c_int,
      [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     ("kllm_gpu_memcpy_d2h", c_int, [c_void_p, c_void_p, c_void_p, c_uint64]),
@@ -277,6 +291,13 @@ class Backend:
         for k, v in kw.items():
             setattr(p, k, v)
         return self.lib.kllm_gpu_build_block_tables(self.ctx, ctypes.byref(p))
+
+    def lm_head(self, **kw) -> int:
+        p = LmHeadParams()
+        p.struct_size = ctypes.sizeof(LmHeadParams)
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return self.lib.kllm_gpu_lm_head_sample(self.ctx, ctypes.byref(p))
 
     def merge(self, m, l, o, num_parts, num_rows, head_dim, out, stream=None) -> int:
         return self.lib.kllm_gpu_merge_partials(self.ctx, m, l, o, num_parts, num_rows,

@@ -181,6 +181,22 @@ class ArrivalConfig:
     staging: int                   # page-locked staging buffers
 
 
+# Vocabulary projection + sampling (the step after attention): Llama-3-8B
+# shapes, bf16 weights ~ N(0, 1/hidden) x 1.5, hidden ~ N(0, 1).
+@dataclass(frozen=True)
+class LmHeadConfig:
+    name: str
+    rows: int
+    hidden: int
+    vocab: int
+    sampling: str                  # "greedy" | "mixed" (temperature / top-k / top-p rows)
+
+
+L3 = LmHeadConfig("l3_lm_head_llama3-8b_b256_greedy", 256, 4096, 128256, "greedy")
+L3S = LmHeadConfig("l3_lm_head_llama3-8b_b256_sampled", 256, 4096, 128256, "mixed")
+LM_HEAD_CONFIGS = {c.name: c for c in (L3, L3S)}
+
+
 W3 = ArrivalConfig("w3_kv_arrival_4096x36k", 4096, 36864, 8)
 ARRIVAL_CONFIGS = {W3.name: W3}
 
