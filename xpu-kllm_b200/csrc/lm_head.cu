@@ -255,6 +255,8 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 
 constexpr int kSampThreads = 256;
 constexpr int kTopKMax = 1024;
+constexpr int kCand = 2048;               // candidate buffer of the top-k search
+constexpr int kTileKeys = 4096;           // tile maxima sortable in shared memory
 static_assert(kSampThreads == kVN, "the in-tile scan gives one column to each thread");
 
 // The float order as unsigned integers (larger key = larger value).
@@ -295,48 +297,101 @@ __device__ float block_scan_f(float x, float *sh, float &total)
 	return before + x;
 }
 
-// Exclusive block scan of one int per thread, and the total.
-__device__ int block_scan_i(int x, int *sh, int &total)
-{
-	const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-	int v = x;
-#pragma unroll
-	for (int o = 1; o < 32; o <<= 1) {
-		const int y = __shfl_up_sync(0xffffffffu, v, o);
-		if (lane >= o)
-			v += y;
-	}
-	if (lane == 31)
-		sh[w] = v;
-	__syncthreads();
-	if (w == 0) {
-		int s = lane < kSampThreads / 32 ? sh[lane] : 0;
-#pragma unroll
-		for (int o = 1; o < 32; o <<= 1) {
-			const int y = __shfl_up_sync(0xffffffffu, s, o);
-			if (lane >= o)
-				s += y;
-		}
-		if (lane < kSampThreads / 32)
-			sh[lane] = s;
-	}
-	__syncthreads();
-	const int before = w ? sh[w - 1] : 0;
-	total = sh[kSampThreads / 32 - 1];
-	__syncthreads();
-	return before + v - x;
-}
-
 struct SampleSmem {
 	float fsh[32];
 	int ish[32];
 	uint32_t hist[256];
-	float cand_v[kTopKMax];
-	int cand_i[kTopKMax];
+	float cand_v[kCand];
+	int cand_i[kCand];
+	uint32_t tkeys[kTileKeys];
 	int found;
+	int count;
 	uint32_t prefix;
 	int remain;
 };
+
+// Bitonic sort of n (a power of two) keys in shared memory, descending.
+__device__ void sort_keys_desc(uint32_t *key, int n)
+{
+	for (int size = 2; size <= n; size <<= 1)
+		for (int stride = size >> 1; stride > 0; stride >>= 1) {
+			for (int j = threadIdx.x; j < n; j += kSampThreads) {
+				const int o = j ^ stride;
+				if (o > j) {
+					const bool desc = (j & size) == 0;
+					const uint32_t a = key[j], b = key[o];
+					if ((a < b) == desc) {
+						key[j] = b;
+						key[o] = a;
+					}
+				}
+			}
+			__syncthreads();
+		}
+}
+
+// Candidates for the k largest of a row, when the tile maxima bound them:
+// the k-th largest tile maximum tau is an element, so at least k elements
+// are >= tau and every one of the k largest is. One pass over the row
+// (16-byte loads, four in flight per thread) collects the elements >= tau;
+// returns their number, or -1 when it exceeds the buffer or k exceeds the
+// tiles (the caller then runs the full radix select).
+__device__ int tile_bound_candidates(const float *lg, int V, const float *pm, int NT, int k,
+				     SampleSmem &sm)
+{
+	if (k > NT || NT > kTileKeys)
+		return -1;
+	int P = 1;
+	while (P < NT)
+		P <<= 1;
+	for (int t = threadIdx.x; t < P; t += kSampThreads)
+		sm.tkeys[t] = t < NT ? order_key(pm[t]) : 0u;
+	if (threadIdx.x == 0)
+		sm.count = 0;
+	__syncthreads();
+	sort_keys_desc(sm.tkeys, P);
+	const uint32_t tau = sm.tkeys[k - 1];
+	__syncthreads();
+	auto take = [&](float v, int i) {
+		if (order_key(v) >= tau) {
+			const int pos = atomicAdd(&sm.count, 1);
+			if (pos < kCand) {
+				sm.cand_v[pos] = v;
+				sm.cand_i[pos] = i;
+			}
+		}
+	};
+	if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(lg) & 15u) == 0) {
+		const float4 *l4 = reinterpret_cast<const float4 *>(lg);
+		const int n4 = V >> 2;
+		for (int base = 0; base < n4; base += 4 * kSampThreads) {
+			float4 x[4];
+#pragma unroll
+			for (int u = 0; u < 4; ++u) {
+				const int j = base + u * kSampThreads + threadIdx.x;
+				x[u] = j < n4 ? l4[j] : make_float4(-CUDART_INF_F, -CUDART_INF_F,
+								    -CUDART_INF_F, -CUDART_INF_F);
+			}
+#pragma unroll
+			for (int u = 0; u < 4; ++u) {
+				const int j = base + u * kSampThreads + threadIdx.x;
+				if (j < n4) {
+					take(x[u].x, 4 * j);
+					take(x[u].y, 4 * j + 1);
+					take(x[u].z, 4 * j + 2);
+					take(x[u].w, 4 * j + 3);
+				}
+			}
+		}
+	} else {
+		for (int i = threadIdx.x; i < V; i += kSampThreads)
+			take(lg[i], i);
+	}
+	__syncthreads();
+	const int n = sm.count;
+	__syncthreads();
+	return n <= kCand ? n : -1;
+}
 
 // Greedy over the tile partials: the largest max, the smallest index on ties.
 __device__ int greedy_token(const float *pm, const int *pa, int NT, SampleSmem &sm)
@@ -458,87 +513,13 @@ __device__ int temperature_token(const kllm_lm_head_args &a, int row, const floa
 	return tok;
 }
 
-// decode_loop.c:118-158: the k largest logits, ordered by (value desc,
-// index asc), then the reference's temperature draw over them.
-__device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, float r,
-			   SampleSmem &sm)
+// Bitonic sort of the first n (a power of two) candidates, descending by
+// value, ascending by index on equal values.
+__device__ void sort_candidates(SampleSmem &sm, int n)
 {
-	const float *lg = a.logits + (size_t)row * a.vocab;
-	const int V = a.vocab;
-	// radix select: the key of the k-th largest logit, 8 bits per pass
-	if (threadIdx.x == 0) {
-		sm.prefix = 0u;
-		sm.remain = k;
-	}
-	__syncthreads();
-	for (int pass = 0; pass < 4; ++pass) {
-		const int shift = 24 - 8 * pass;
-		const uint32_t hi_mask = pass ? (0xFFFFFFFFu << (32 - 8 * pass)) : 0u;
-		for (int i = threadIdx.x; i < 256; i += kSampThreads)
-			sm.hist[i] = 0u;
-		__syncthreads();
-		const uint32_t prefix = sm.prefix;
-		for (int i = threadIdx.x; i < V; i += kSampThreads) {
-			const uint32_t key = order_key(lg[i]);
-			if ((key & hi_mask) == prefix)
-				atomicAdd(&sm.hist[(key >> shift) & 0xFFu], 1u);
-		}
-		__syncthreads();
-		if (threadIdx.x == 0) {
-			int rem = sm.remain;
-			int bin = 255;
-			for (; bin > 0; --bin) {
-				if ((int)sm.hist[bin] >= rem)
-					break;
-				rem -= (int)sm.hist[bin];
-			}
-			sm.prefix = prefix | ((uint32_t)bin << shift);
-			sm.remain = rem;            // how many of the k-th key's equals to take
-		}
-		__syncthreads();
-	}
-	const uint32_t kth = sm.prefix;
-	const int need_eq = sm.remain;
-	// ordered pass: every key above kth, and the first need_eq keys equal to it
-	int n_gt = 0, n_eq = 0;
-	for (int base = 0; base < V; base += kSampThreads) {
-		const int i = base + threadIdx.x;
-		const uint32_t key = i < V ? order_key(lg[i]) : 0u;
-		const int gt = i < V && key > kth, eq = i < V && key == kth;
-		int tg, te;
-		const int pg = block_scan_i(gt, sm.ish, tg);
-		const int pe = block_scan_i(eq, sm.ish, te);
-		if (gt)
-			sm.cand_i[n_gt + pg] = i;
-		if (eq && n_eq + pe < need_eq)
-			sm.cand_v[n_eq + pe] = __int_as_float(i);   // parked; placed below
-		n_gt += tg;
-		n_eq += te;
-		__syncthreads();
-	}
-	// candidates: [0, n_gt) above kth (index order), then need_eq equals
-	const int n_gt_sel = k - need_eq;
-	for (int j = threadIdx.x; j < need_eq; j += kSampThreads) {
-		const int i = __float_as_int(sm.cand_v[j]);
-		sm.cand_i[n_gt_sel + j] = i;
-	}
-	__syncthreads();
-	int P = 1;
-	while (P < k)
-		P <<= 1;
-	for (int j = threadIdx.x; j < P; j += kSampThreads) {
-		if (j < k) {
-			sm.cand_v[j] = lg[sm.cand_i[j]];
-		} else {
-			sm.cand_v[j] = -CUDART_INF_F;
-			sm.cand_i[j] = 0x7fffffff;
-		}
-	}
-	__syncthreads();
-	// bitonic sort, descending by value then ascending by index
-	for (int size = 2; size <= P; size <<= 1)
+	for (int size = 2; size <= n; size <<= 1)
 		for (int stride = size >> 1; stride > 0; stride >>= 1) {
-			for (int j = threadIdx.x; j < P; j += kSampThreads) {
+			for (int j = threadIdx.x; j < n; j += kSampThreads) {
 				const int o = j ^ stride;
 				if (o > j) {
 					const bool desc = (j & size) == 0;
@@ -555,7 +536,12 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 			}
 			__syncthreads();
 		}
-	// the reference's draw over the sorted list, sequential as it runs it
+}
+
+// The reference's temperature draw over the first k sorted candidates
+// (decode_loop.c:71-113 on the top-k list), sequential as it runs it.
+__device__ int draw_sorted(SampleSmem &sm, int k, float T, float r)
+{
 	if (threadIdx.x == 0) {
 		int res = 0;
 		if (T > 0.f) {
@@ -585,6 +571,133 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 	const int tok = sm.found;
 	__syncthreads();
 	return tok;
+}
+
+// decode_loop.c:118-158: the k largest logits, ordered by (value desc,
+// index asc), then the reference's temperature draw over them.
+__device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, float r,
+			   SampleSmem &sm)
+{
+	const float *lg = a.logits + (size_t)row * a.vocab;
+	const int V = a.vocab;
+	const int NT = (V + kVN - 1) / kVN;
+	const int nc = tile_bound_candidates(lg, V, a.part_m + (size_t)row * NT, NT, k, sm);
+	if (nc >= 0) {
+		// the candidates hold the k largest: sort them all, keep the first k
+		int P = 1;
+		while (P < nc)
+			P <<= 1;
+		for (int j = nc + threadIdx.x; j < P; j += kSampThreads) {
+			sm.cand_v[j] = -CUDART_INF_F;
+			sm.cand_i[j] = 0x7fffffff;
+		}
+		__syncthreads();
+		sort_candidates(sm, P);
+		return draw_sorted(sm, k, T, r);
+	}
+	// radix select: the key of the k-th largest logit, 8 bits per pass; every
+	// loop is warp-uniform (ballots), histogram adds aggregated per bin
+	const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+	if (threadIdx.x == 0) {
+		sm.prefix = 0u;
+		sm.remain = k;
+	}
+	__syncthreads();
+	for (int pass = 0; pass < 4; ++pass) {
+		const int shift = 24 - 8 * pass;
+		const uint32_t hi_mask = pass ? (0xFFFFFFFFu << (32 - 8 * pass)) : 0u;
+		for (int i = threadIdx.x; i < 256; i += kSampThreads)
+			sm.hist[i] = 0u;
+		__syncthreads();
+		const uint32_t prefix = sm.prefix;
+		for (int base = 0; base < V; base += kSampThreads) {
+			const int i = base + threadIdx.x;
+			const uint32_t key = i < V ? order_key(lg[i]) : 0u;
+			const bool hit = i < V && (key & hi_mask) == prefix;
+			const unsigned act = __ballot_sync(0xffffffffu, hit);
+			if (hit) {
+				const uint32_t bin = (key >> shift) & 0xFFu;
+				const unsigned peers = __match_any_sync(act, bin);
+				if ((int)(__ffs(peers) - 1) == lane)
+					atomicAdd(&sm.hist[bin], (uint32_t)__popc(peers));
+			}
+		}
+		__syncthreads();
+		if (threadIdx.x == 0) {
+			int rem = sm.remain;
+			int bin = 255;
+			for (; bin > 0; --bin) {
+				if ((int)sm.hist[bin] >= rem)
+					break;
+				rem -= (int)sm.hist[bin];
+			}
+			sm.prefix = prefix | ((uint32_t)bin << shift);
+			sm.remain = rem;            // how many of the k-th key's equals to take
+		}
+		__syncthreads();
+	}
+	const uint32_t kth = sm.prefix;
+	const int need_eq = sm.remain;
+	// ordered selection, every key above kth and the first need_eq equal to
+	// it: warp w scans its contiguous segment twice (count, then place by
+	// ballot rank), one prefix over the warps in between
+	constexpr int kW = kSampThreads / 32;
+	const int seg = ((V + kW - 1) / kW + 31) & ~31;
+	const int s0 = min(V, w * seg), s1 = min(V, s0 + seg);
+	int cg = 0, ce = 0;
+	for (int base = s0; base < s1; base += 32) {
+		const int i = base + lane;
+		const uint32_t key = i < s1 ? order_key(lg[i]) : 0u;
+		cg += __popc(__ballot_sync(0xffffffffu, i < s1 && key > kth));
+		ce += __popc(__ballot_sync(0xffffffffu, i < s1 && key == kth));
+	}
+	if (lane == 0) {
+		sm.ish[w] = cg;
+		sm.ish[kW + w] = ce;
+	}
+	__syncthreads();
+	int rg = 0, re = 0;
+	for (int j = 0; j < w; ++j) {
+		rg += sm.ish[j];
+		re += sm.ish[kW + j];
+	}
+	const unsigned lt = (1u << lane) - 1u;
+	int *eq_idx = reinterpret_cast<int *>(sm.cand_v);    // parked equal-key indices
+	for (int base = s0; base < s1; base += 32) {
+		const int i = base + lane;
+		const uint32_t key = i < s1 ? order_key(lg[i]) : 0u;
+		const bool gt = i < s1 && key > kth, eq = i < s1 && key == kth;
+		const unsigned bg = __ballot_sync(0xffffffffu, gt), bq = __ballot_sync(0xffffffffu, eq);
+		if (gt)
+			sm.cand_i[rg + __popc(bg & lt)] = i;
+		if (eq) {
+			const int pos = re + __popc(bq & lt);
+			if (pos < need_eq)
+				eq_idx[pos] = i;
+		}
+		rg += __popc(bg);
+		re += __popc(bq);
+	}
+	__syncthreads();
+	// candidates: [0, k - need_eq) above kth (index order), then need_eq equals
+	const int n_gt_sel = k - need_eq;
+	for (int j = threadIdx.x; j < need_eq; j += kSampThreads)
+		sm.cand_i[n_gt_sel + j] = eq_idx[j];
+	__syncthreads();
+	int P = 1;
+	while (P < k)
+		P <<= 1;
+	for (int j = threadIdx.x; j < P; j += kSampThreads) {
+		if (j < k) {
+			sm.cand_v[j] = lg[sm.cand_i[j]];
+		} else {
+			sm.cand_v[j] = -CUDART_INF_F;
+			sm.cand_i[j] = 0x7fffffff;
+		}
+	}
+	__syncthreads();
+	sort_candidates(sm, P);
+	return draw_sorted(sm, k, T, r);
 }
 
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const kllm_lm_head_args a)
