@@ -361,15 +361,39 @@ def run_kllm(args) -> None:
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
 
+    # copies on their own streams (uploads, read-backs), overlapping the
+    # decode of neighbouring layers; events order each layer's upload ->
+    # decode -> read-back, and a layer's buffers are reused only after the
+    # previous step's decode / read-back of that layer finished
+    up_s, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    L = cfg.layers
+    ev_in = [torch.cuda.Event() for _ in range(L)]
+    ev_done = [torch.cuda.Event() for _ in range(L)]
+    ev_out = [torch.cuda.Event() for _ in range(L)]
+    ev_go = torch.cuda.Event()
+    ev_end = torch.cuda.Event()
+
     def e2e_step():
         lib.kllm_gpu_memcpy_h2d_async(ctx, rig.seq_lens.data_ptr(), host_lens.data_ptr(),
                                       host_lens.numel() * 4, sp)
-        for layer in range(cfg.layers):
+        ev_go.record(stream)
+        up_s.wait_event(ev_go)
+        for layer in range(L):
+            up_s.wait_event(ev_done[layer])          # the previous step read q[layer]
             lib.kllm_gpu_memcpy_h2d_async(ctx, rig.q[layer].data_ptr(),
-                                          host_q[layer].data_ptr(), qb, sp)
+                                          host_q[layer].data_ptr(), qb, up_s.cuda_stream)
+            ev_in[layer].record(up_s)
+        for layer in range(L):
+            stream.wait_event(ev_in[layer])
+            stream.wait_event(ev_out[layer])         # the previous step's read-back of out
             rig.launch(layer, sp)
+            ev_done[layer].record(stream)
+            down_s.wait_event(ev_done[layer])
             lib.kllm_gpu_memcpy_d2h_async(ctx, host_o[layer].data_ptr(),
-                                          rig.out[layer].data_ptr(), qb, sp)
+                                          rig.out[layer].data_ptr(), qb, down_s.cuda_stream)
+            ev_out[layer].record(down_s)
+        ev_end.record(down_s)
+        stream.wait_event(ev_end)                    # the step ends with its last read-back
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -380,6 +404,8 @@ def run_kllm(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
+    if not torch.equal(host_o[L - 1][:4].to(rig.out.device), rig.out[L - 1][:4]):
+        raise RuntimeError("end-to-end read-back differs from the device output")
 
     my_bytes = rig.step_bytes()
     stats = torch.tensor([elapsed_ms, e2e_ms, float(my_bytes), float(rig.B),
