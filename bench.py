@@ -373,11 +373,12 @@ def run_kllm(args) -> None:
     ev_go = torch.cuda.Event()
     ev_end = torch.cuda.Event()
 
-    def e2e_step():
+    def e2e_step(first=False):
         lib.kllm_gpu_memcpy_h2d_async(ctx, rig.seq_lens.data_ptr(), host_lens.data_ptr(),
                                       host_lens.numel() * 4, sp)
-        ev_go.record(stream)
-        up_s.wait_event(ev_go)
+        if first:                                    # no copy starts before the region opens
+            ev_go.record(stream)
+            up_s.wait_event(ev_go)
         for layer in range(L):
             up_s.wait_event(ev_done[layer])          # the previous step read q[layer]
             lib.kllm_gpu_memcpy_h2d_async(ctx, rig.q[layer].data_ptr(),
@@ -399,8 +400,8 @@ def run_kllm(args) -> None:
         e2e_step()
     barrier()
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    for i in range(args.steps):
+        e2e_step(i == 0)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -733,32 +734,62 @@ def run_prefill(args) -> None:
     assert int(rig.err.item()) == 0, f"prefill error word {int(rig.err.item()):#x}"
 
     # end to end through the C ABI: pinned host Q/K/V in, O out, one
-    # prefill_v2 call with append per step
+    # prefill_v2 call with append per step. Two device buffer sets alternate
+    # by step, so step s + 1's uploads (their own stream) and step s - 1's
+    # read-back (another stream) overlap step s's prefill; events order
+    # upload -> prefill -> read-back per buffer set and hold a set until its
+    # previous read-back finished
     hq_, hk_, hv_ = (x.cpu().pin_memory() for x in (rig.q, rig.k, rig.v))
     ho = torch.empty_like(rig.out, device="cpu").pin_memory()
     lib, ctx = be.lib, be.ctx
-    dq = torch.empty_like(rig.q)
-    dk = torch.empty_like(rig.k)
-    dv = torch.empty_like(rig.v)
-    nb = {id(hq_): rig.q.numel() * 2, id(hk_): rig.k.numel() * 2, id(hv_): rig.v.numel() * 2}
+    sets = [tuple(torch.empty_like(x) for x in (rig.q, rig.k, rig.v, rig.out)) for _ in range(2)]
+    nbytes = (rig.q.numel() * 2, rig.k.numel() * 2, rig.v.numel() * 2)
+    up_s, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_go, ev_end = torch.cuda.Event(), torch.cuda.Event()
+    n_e2e = [0]
 
-    def e2e_step():
-        for h, d in ((hq_, dq), (hk_, dk), (hv_, dv)):
-            lib.kllm_gpu_memcpy_h2d_async(ctx, d.data_ptr(), h.data_ptr(), nb[id(h)], sp)
-        rig.prefill(sp, append=1, q=dq.data_ptr(), k=dk.data_ptr(), v=dv.data_ptr())
-        lib.kllm_gpu_memcpy_d2h_async(ctx, ho.data_ptr(), rig.out.data_ptr(),
-                                      rig.out.numel() * 2, sp)
+    def e2e_step(first=False):
+        b = n_e2e[0] & 1
+        n_e2e[0] += 1
+        dq, dk, dv, do = sets[b]
+        if first:                                    # no copy starts before the region opens
+            ev_go.record(stream)
+            up_s.wait_event(ev_go)
+        up_s.wait_event(ev_done[b])                  # the set's previous prefill read it
+        for h, d, n in ((hq_, dq, nbytes[0]), (hk_, dk, nbytes[1]), (hv_, dv, nbytes[2])):
+            lib.kllm_gpu_memcpy_h2d_async(ctx, d.data_ptr(), h.data_ptr(), n, up_s.cuda_stream)
+        ev_in[b].record(up_s)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])                 # the set's previous read-back of O
+        rig.prefill(sp, append=1, q=dq.data_ptr(), k=dk.data_ptr(), v=dv.data_ptr(),
+                    out=do.data_ptr())
+        ev_done[b].record(stream)
+        down_s.wait_event(ev_done[b])
+        lib.kllm_gpu_memcpy_d2h_async(ctx, ho.data_ptr(), do.data_ptr(), rig.out.numel() * 2,
+                                      down_s.cuda_stream)
+        ev_out[b].record(down_s)
+
+    def e2e_drain():
+        ev_end.record(down_s)
+        stream.wait_event(ev_end)                    # every read-back is inside the region
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
+    e2e_drain()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    for i in range(args.steps):
+        e2e_step(i == 0)
+    e2e_drain()
     e1.record(stream)
     torch.cuda.synchronize()
+    if not torch.equal(ho[:2].to(rig.out.device), sets[(n_e2e[0] - 1) & 1][3][:2]):
+        raise RuntimeError("end-to-end read-back differs from the device output")
     te_ms = e0.elapsed_time(e1)
 
     cpu = None
@@ -805,7 +836,7 @@ def run_prefill(args) -> None:
                                 "kernel": "append_kernel", "launch_ms": round(ap_ms, 4)},
             "e2e": {"value": round(rig.n_tok * args.steps / (te_ms * 1e-3), 1),
                     "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(sum(nb.values())),
+                    "h2d_bytes_per_step": int(sum(nbytes)),
                     "d2h_bytes_per_step": int(rig.out.numel() * 2)},
             "gpu_launches": int(launches),
             "clocks": clocks,
@@ -1202,13 +1233,14 @@ def run_lm_head(args) -> None:
     st = torch.cuda.current_stream()
     sp = st.cuda_stream
 
-    def step(hptr=None):
+    def step(hptr=None, tptr=None):
         rc = be.lm_head(hidden=hptr or hid.data_ptr(), weight=w.data_ptr(), num_rows=R,
                         hidden_dim=H, vocab=V, logits=logits.data_ptr(),
                         method=meth.data_ptr() if meth is not None else None,
                         temperature=temp.data_ptr() if temp is not None else None,
                         top_k=topk.data_ptr() if topk is not None else None,
-                        uniform=uni.data_ptr(), tokens=tok.data_ptr(), workspace=ws.data_ptr(),
+                        uniform=uni.data_ptr(), tokens=tptr or tok.data_ptr(),
+                        workspace=ws.data_ptr(),
                         workspace_bytes=ws_b, err_word=err.data_ptr(), stream=sp)
         if rc != 0:
             raise RuntimeError(f"lm_head failed: {rc}")
@@ -1234,23 +1266,52 @@ def run_lm_head(args) -> None:
     clocks = clk.stop()
     launches = be.stats().launches - launches0
     t_ms = e0.elapsed_time(e1)
-    # end to end through the C ABI: pinned hidden states in, tokens out
+    # end to end through the C ABI: pinned hidden states in, tokens out; two
+    # hidden-state buffers alternate by step so the next step's upload (its
+    # own stream) overlaps this step's projection, ordered by events
     h_h = hid.cpu().pin_memory()
     h_t = torch.empty(R, dtype=torch.int32).pin_memory()
-    d_h = torch.empty_like(hid)
+    d_hs = [torch.empty_like(hid) for _ in range(2)]
+    d_ts = [torch.empty_like(tok) for _ in range(2)]
     lib, ctx = be.lib, be.ctx
+    up_s, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_tok = [torch.cuda.Event() for _ in range(2)]
+    ev_go, ev_end = torch.cuda.Event(), torch.cuda.Event()
+    n_e2e = [0]
 
-    def e2e_step():
-        lib.kllm_gpu_memcpy_h2d_async(ctx, d_h.data_ptr(), h_h.data_ptr(), R * H * 2, sp)
-        step(d_h.data_ptr())
-        lib.kllm_gpu_memcpy_d2h_async(ctx, h_t.data_ptr(), tok.data_ptr(), R * 4, sp)
+    def e2e_step(first=False):
+        b = n_e2e[0] & 1
+        n_e2e[0] += 1
+        if first:                                    # no copy starts before the region opens
+            ev_go.record(st)
+            up_s.wait_event(ev_go)
+        up_s.wait_event(ev_done[b])                  # the buffer's previous projection read it
+        lib.kllm_gpu_memcpy_h2d_async(ctx, d_hs[b].data_ptr(), h_h.data_ptr(), R * H * 2,
+                                      up_s.cuda_stream)
+        ev_in[b].record(up_s)
+        st.wait_event(ev_in[b])
+        st.wait_event(ev_tok[b])                     # the buffer's previous tokens were read
+        step(d_hs[b].data_ptr(), d_ts[b].data_ptr())
+        ev_done[b].record(st)
+        down_s.wait_event(ev_done[b])
+        lib.kllm_gpu_memcpy_d2h_async(ctx, h_t.data_ptr(), d_ts[b].data_ptr(), R * 4,
+                                      down_s.cuda_stream)
+        ev_tok[b].record(down_s)
+
+    def e2e_drain():
+        ev_end.record(down_s)
+        st.wait_event(ev_end)
 
     for _ in range(args.warmup):
         e2e_step()
+    e2e_drain()
     torch.cuda.synchronize()
     e0.record(st)
-    for _ in range(args.steps):
-        e2e_step()
+    for i in range(args.steps):
+        e2e_step(i == 0)
+    e2e_drain()
     e1.record(st)
     torch.cuda.synchronize()
     te_ms = e0.elapsed_time(e1)

@@ -35,3 +35,26 @@ def test_reference_arm_json_line():
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["warmup"] >= 3
+
+
+def test_reference_arm_table_build():
+    """The block-table build's reference arm runs the reference's own path
+    (OpenSSL SHA256 keys + cache_index.c lookups) when oracle/_ref has it."""
+    import pytest
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    line = _run("--impl", "reference", "--config", "t5_tables_b16_2048_prefix1024", "--steps",
+                "2", "--warmup", "3")
+    if oracle.ref_index_lib() is None:
+        assert "unavailable" in line
+        pytest.skip("reference index library not built")
+    assert line["impl"] == "reference" and line["unit"] == "blocks/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "reference"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_reference_arm_unavailable_lines():
+    """Paths the reference only stubs print the contract's unavailable line."""
+    for cfg in ("w3_kv_arrival_4096x36k", "l3_lm_head_llama3-8b_b256_greedy"):
+        line = _run("--impl", "reference", "--config", cfg)
+        assert line["impl"] == "reference" and line["unavailable"]
