@@ -144,7 +144,9 @@ int kllm_gpu_paged_attention_cuda(
  *   [block_size][head_dim/8] E4M3 scale bytes (one scale per 8 consecutive
  *   elements along head_dim, userspace/compute/mx_dequant.h:27). Real value =
  *   e4m3(payload) * e4m3(scale), decoded as userspace/compute/mx_dequant.h:30-55
- *   (0x7F/0xFF decode to +-480). V page alike.
+ *   (0x7F/0xFF decode to +-480; the decode kernel converts payloads with the
+ *   hardware OCP E4M3 conversion, which reads payload 0x7F/0xFF as NaN; the
+ *   append never writes them). V page alike.
  *
  * KLLM_KV_MX_BF16_COMPAT: the reference's own MX layout
  *   (userspace/compute/mx_dequant.h:10-16): sections of [block_size][head_dim]
