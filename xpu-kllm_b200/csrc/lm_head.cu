@@ -610,16 +610,24 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 			sm.hist[i] = 0u;
 		__syncthreads();
 		const uint32_t prefix = sm.prefix;
-		for (int base = 0; base < V; base += kSampThreads) {
-			const int i = base + threadIdx.x;
-			const uint32_t key = i < V ? order_key(lg[i]) : 0u;
-			const bool hit = i < V && (key & hi_mask) == prefix;
-			const unsigned act = __ballot_sync(0xffffffffu, hit);
-			if (hit) {
-				const uint32_t bin = (key >> shift) & 0xFFu;
-				const unsigned peers = __match_any_sync(act, bin);
-				if ((int)(__ffs(peers) - 1) == lane)
-					atomicAdd(&sm.hist[bin], (uint32_t)__popc(peers));
+		for (int base = 0; base < V; base += 4 * kSampThreads) {
+			uint32_t key4[4];                 // four loads in flight per thread
+#pragma unroll
+			for (int u = 0; u < 4; ++u) {
+				const int i = base + u * kSampThreads + threadIdx.x;
+				key4[u] = i < V ? order_key(lg[i]) : 0u;
+			}
+#pragma unroll
+			for (int u = 0; u < 4; ++u) {
+				const int i = base + u * kSampThreads + threadIdx.x;
+				const bool hit = i < V && (key4[u] & hi_mask) == prefix;
+				const unsigned act = __ballot_sync(0xffffffffu, hit);
+				if (hit) {
+					const uint32_t bin = (key4[u] >> shift) & 0xFFu;
+					const unsigned peers = __match_any_sync(act, bin);
+					if ((int)(__ffs(peers) - 1) == lane)
+						atomicAdd(&sm.hist[bin], (uint32_t)__popc(peers));
+				}
 			}
 		}
 		__syncthreads();
@@ -645,11 +653,19 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 	const int seg = ((V + kW - 1) / kW + 31) & ~31;
 	const int s0 = min(V, w * seg), s1 = min(V, s0 + seg);
 	int cg = 0, ce = 0;
-	for (int base = s0; base < s1; base += 32) {
-		const int i = base + lane;
-		const uint32_t key = i < s1 ? order_key(lg[i]) : 0u;
-		cg += __popc(__ballot_sync(0xffffffffu, i < s1 && key > kth));
-		ce += __popc(__ballot_sync(0xffffffffu, i < s1 && key == kth));
+	for (int base = s0; base < s1; base += 128) {
+		uint32_t key4[4];
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {
+			const int i = base + 32 * u + lane;
+			key4[u] = i < s1 ? order_key(lg[i]) : 0u;
+		}
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {
+			const int i = base + 32 * u + lane;
+			cg += __popc(__ballot_sync(0xffffffffu, i < s1 && key4[u] > kth));
+			ce += __popc(__ballot_sync(0xffffffffu, i < s1 && key4[u] == kth));
+		}
 	}
 	if (lane == 0) {
 		sm.ish[w] = cg;
@@ -663,20 +679,29 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 	}
 	const unsigned lt = (1u << lane) - 1u;
 	int *eq_idx = reinterpret_cast<int *>(sm.cand_v);    // parked equal-key indices
-	for (int base = s0; base < s1; base += 32) {
-		const int i = base + lane;
-		const uint32_t key = i < s1 ? order_key(lg[i]) : 0u;
-		const bool gt = i < s1 && key > kth, eq = i < s1 && key == kth;
-		const unsigned bg = __ballot_sync(0xffffffffu, gt), bq = __ballot_sync(0xffffffffu, eq);
-		if (gt)
-			sm.cand_i[rg + __popc(bg & lt)] = i;
-		if (eq) {
-			const int pos = re + __popc(bq & lt);
-			if (pos < need_eq)
-				eq_idx[pos] = i;
+	for (int base = s0; base < s1; base += 128) {
+		uint32_t key4[4];
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {
+			const int i = base + 32 * u + lane;
+			key4[u] = i < s1 ? order_key(lg[i]) : 0u;
 		}
-		rg += __popc(bg);
-		re += __popc(bq);
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {                   // index order: u, then lane
+			const int i = base + 32 * u + lane;
+			const bool gt = i < s1 && key4[u] > kth, eq = i < s1 && key4[u] == kth;
+			const unsigned bg = __ballot_sync(0xffffffffu, gt);
+			const unsigned bq = __ballot_sync(0xffffffffu, eq);
+			if (gt)
+				sm.cand_i[rg + __popc(bg & lt)] = i;
+			if (eq) {
+				const int pos = re + __popc(bq & lt);
+				if (pos < need_eq)
+					eq_idx[pos] = i;
+			}
+			rg += __popc(bg);
+			re += __popc(bq);
+		}
 	}
 	__syncthreads();
 	// candidates: [0, k - need_eq) above kth (index order), then need_eq equals
