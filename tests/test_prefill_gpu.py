@@ -155,3 +155,19 @@ def test_prefill_c5_shared_prefix_sampled(be):
     want = _oracle_rows(hc, ctx_lens, cu, q, k, v, rows=rows)
     got, _ = _run(be, *case)
     _check(got, want, "C5")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_MX_FP8, wl.KV_BF16])
+@pytest.mark.parametrize("block", [32, 128])
+def test_prefill_edges(be, kv, block):
+    """An empty chunk, one-token chunks over short and empty contexts, a
+    context that ends one past a page, chunks that cross tile boundaries;
+    pages of 32 and 128 tokens; K/V magnitudes scaled per (sequence, head)
+    by 0.5 .. 4 as in the C2 workload."""
+    cfg = replace(wl.C2, kv_dtype=kv, block=block)
+    case = _case(cfg, ctx_lens=[5, 0, 257, 31, 1, 0], chunk_lens=[1, 0, 65, 300, 128, 1],
+                 seed=9)
+    hc, ctx_lens, chunk_lens, cu, q, k, v = case
+    want = _oracle_rows(hc, ctx_lens, cu, q, k, v)
+    got, _ = _run(be, *case)
+    _check(got, want, f"edges kv={kv} block={block}")
