@@ -15,14 +15,19 @@
  * block's obj_key is resolved to its record through an index with the
  * cache index's layout and probe (struct kllm_gpu_index_entry, slot_index =
  * record number), given by kllm_wavefront_set_index. Resolution happens in
- * submit, on the caller's thread; one I/O thread reads the records into
- * page-locked staging buffers and copies them to vram_dest_addr on its own
- * CUDA stream; completion is a CUDA event that poll queries.
+ * submit, on the caller's thread, which also checks that every
+ * vram_dest_addr range lies in one device allocation on the context's GPU
+ * (a block that does not is reported failed). Up to four I/O threads (one
+ * per two staging buffers) split each wavefront's blocks, read the records
+ * into their own page-locked staging buffers, copy each buffer to the GPU
+ * in one piece and place its records with one kernel launch, on their own
+ * CUDA streams; completion is one CUDA event per thread that poll queries,
+ * and jobs are reported in submit order.
  *
  * Return conventions: submit 0 / -1 (reference), poll the number of
  * completions filled. Extensions return 0 or a negative KLLM_E* code.
  * Threading: submit, poll and wait are called from one thread (the
- * reactor's); the context owns its I/O thread.
+ * reactor's); the context owns its I/O threads.
  */
 #ifndef KLLM_WAVEFRONT_H
 #define KLLM_WAVEFRONT_H
@@ -86,8 +91,11 @@ int kllm_wavefront_poll(struct kllm_wavefront_ctx *ctx,
 
 /* ---- Part 2: extensions ------------------------------------------------- */
 
-/* As kllm_wavefront_create with the device, the largest block (staging
- * buffer size) and the number of staging buffers (2..64) chosen. */
+/* As kllm_wavefront_create with the device, the largest block (at most
+ * 1 GiB) and the number of staging buffers (2..64) chosen; the buffers are
+ * shared out over min(4, staging_buffers / 2) I/O threads, and each holds
+ * max(largest block, 2 MiB) in page-locked host memory plus as much device
+ * memory. */
 struct kllm_wavefront_ctx *kllm_wavefront_create2(const char *store_path, int device,
 						  uint64_t max_block_bytes, int staging_buffers);
 /* The key -> record map: entries (host memory, [capacity], capacity a

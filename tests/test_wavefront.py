@@ -5,8 +5,10 @@ nvme_ep_wavefront.c:74-104). CPU: the library exports every symbol the
 header declares, the structs have the reference's layout, and with no device
 the context is refused instead of spinning. GPU: blocks resolved by key
 through the store index land in device memory byte for byte; missing keys
-are reported as failed; completions come back in submit order; a full queue
-refuses instead of blocking; a wait with nothing pending ends at its bound."""
+and destinations outside this GPU's device memory (host memory, an unmapped
+address) are reported as failed without being written; completions come back
+in submit order; a full queue refuses instead of blocking; a wait with
+nothing pending ends at its bound."""
 from __future__ import annotations
 
 import ctypes
@@ -103,7 +105,8 @@ def test_blocks_arrive_in_vram(tmp_path):
         dev = torch.zeros((R + 60) * RB, dtype=torch.uint8, device="cuda")
         base = dev.data_ptr()
         rng = np.random.default_rng(2)
-        want = {}                     # device slot -> record (or None: must stay zero)
+        host_buf = np.zeros(RB, dtype=np.uint8)         # not a device destination
+        want = {}                     # device slot -> record (or None: not checked)
         n_wf, expect = 9, []
         slot = 0
         for w in range(n_wf):
@@ -117,8 +120,11 @@ def test_blocks_arrive_in_vram(tmp_path):
                 ctypes.memmove(d.obj_key, keys[rec], 32)
                 d.vram_dest_addr = base + slot * RB
                 d.block_size = RB if i % 7 else RB - 100  # a short block now and then
-                want[slot] = (rec if rec < R else None, d.block_size)
-                failed += rec >= R
+                bad_dst = w == 3 and i % 5 == 1
+                if bad_dst:
+                    d.vram_dest_addr = host_buf.ctypes.data if i % 2 else 4096
+                want[slot] = (rec if rec < R and not bad_dst else None, d.block_size)
+                failed += rec >= R or bad_dst
                 slot = (slot + 1) % (R + 60)
             assert lib.kllm_wavefront_submit(wf_ctx, ctypes.byref(wf)) == 0
             expect.append((1000 + w, nb - failed, failed))
@@ -131,6 +137,7 @@ def test_blocks_arrive_in_vram(tmp_path):
                     for i in range(n)]
         assert got == expect                            # submit order, exact counts
         assert lib.kllm_wavefront_error(wf_ctx) == 0
+        assert not host_buf.any()
         torch.cuda.synchronize()
         host = dev.cpu().numpy().reshape(R + 60, RB)
         for s, (rec, nbytes) in want.items():

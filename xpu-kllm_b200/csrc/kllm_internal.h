@@ -182,6 +182,19 @@ struct kllm_lm_head_args {
 int kllm_lm_head_tiles(int vocab);
 int kllm_lm_head_launch(const struct kllm_lm_head_args *a, void *stream);
 
+/* Block arrival: one chunk of records already copied to device memory at
+ * src_dev; record i (bytes[i] at src_dev + off[i], off 16-byte aligned) goes
+ * to dst[i], a range the host checked lies in device memory of this GPU. */
+#define KLLM_WF_SCATTER_MAX 64
+struct kllm_wf_scatter {
+	uint32_t n;
+	uint32_t reserved;
+	uint64_t dst[KLLM_WF_SCATTER_MAX];
+	uint32_t bytes[KLLM_WF_SCATTER_MAX];
+	uint32_t off[KLLM_WF_SCATTER_MAX];
+};
+int kllm_wf_scatter_launch(const struct kllm_wf_scatter *s, const void *src_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

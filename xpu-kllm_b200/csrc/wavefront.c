@@ -7,13 +7,20 @@
  * submit (caller's thread): resolves every block's obj_key through the
  * caller's index (the cache index probe: bucket = first four key bytes,
  * little-endian, masked; linear probe to the first empty entry) to a record
- * offset, and queues the job. One I/O thread per context takes jobs in
- * order: pread of each record into the next page-locked staging buffer
- * (after that buffer's previous copy has completed), cudaMemcpyAsync to the
- * destination on the context's stream, an event per buffer and one per job.
- * poll (caller's thread) reports jobs whose event completed, in submit
- * order. Nothing here waits without a bound except the I/O thread on a
- * staging buffer's own earlier copy.
+ * offset, and queues the job. Up to four I/O threads per context take every
+ * job in order, thread t the blocks i with i % threads == t. A thread
+ * preads its blocks of a job into its next page-locked staging chunk (after
+ * that chunk's previous use has completed), copies the chunk to device
+ * memory with one cudaMemcpyAsync on its own stream, and launches one
+ * scatter kernel that places each record at its destination
+ * (wavefront_scatter.cu); an event per chunk and one per (job, thread).
+ * Per-block copies were bound by the driver's per-call cost, which one copy
+ * and one launch per chunk amortise. Because a kernel (not the copy engine)
+ * writes the destinations, submit checks each one: device memory of this
+ * context's GPU, inside one allocation; a block that fails is reported as
+ * failed. poll (caller's thread) reports a job once every thread has passed
+ * it and its events completed, in submit order. Nothing here waits without
+ * a bound except an I/O thread on a staging chunk's own earlier use.
  */
 #define _GNU_SOURCE
 #include <errno.h>
@@ -24,14 +31,18 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <cuda.h>
 #include <cuda_runtime_api.h>
 
 #include "kllm_gpu.h"
+#include "kllm_internal.h"
 #include "kllm_wavefront.h"
 
 #define WF_QUEUE 64
-
-enum { JOB_FREE = 0, JOB_QUEUED, JOB_ISSUED };
+#define WF_MAX_THREADS 4
+#define WF_MAX_STAGE 16                 /* staging chunks per I/O thread */
+#define WF_MIN_CHUNK (2u << 20)         /* a chunk holds many small blocks */
+#define WF_RANGES 4                     /* allocations remembered within one submit */
 
 struct wf_item {
 	uint64_t off;
@@ -41,33 +52,44 @@ struct wf_item {
 };
 
 struct wf_job {
-	int state;
 	uint64_t seq;
 	uint64_t t0;
-	uint32_t n, failed;
-	uint64_t bytes;
-	cudaEvent_t done;
+	uint32_t n;
+	uint32_t failed;                /* unresolved at submit, then added by the threads */
+	uint64_t bytes;                 /* added by the threads */
+	cudaEvent_t done[WF_MAX_THREADS];
 	struct wf_item items[KLLM_WAVEFRONT_MAX_BLOCKS];
+};
+
+struct kllm_wavefront_ctx;
+
+struct wf_worker {
+	struct kllm_wavefront_ctx *c;
+	int id;
+	pthread_t thr;
+	int started;
+	cudaStream_t stream;
+	int n_stage, next;
+	uint8_t *stage[WF_MAX_STAGE];           /* page-locked host chunks */
+	uint8_t *dev_stage[WF_MAX_STAGE];       /* their device copies */
+	cudaEvent_t stage_ev[WF_MAX_STAGE];     /* the chunk's scatter has finished */
+	uint32_t head;                  /* next job this thread issues (under mu) */
 };
 
 struct kllm_wavefront_ctx {
 	int fd;
 	int device;
-	cudaStream_t stream;
 	const struct kllm_gpu_index_entry *index;
 	uint32_t capacity;
 	uint64_t record_bytes, base_offset;
-	int n_stage;
-	uint64_t stage_bytes;
-	uint8_t *stage[64];
-	cudaEvent_t stage_ev[64];
-	int stage_next;
+	uint64_t stage_bytes;                   /* largest block */
+	uint64_t chunk_bytes;                   /* staging chunk */
+	CUresult (*get_range)(CUdeviceptr *, size_t *, CUdeviceptr);
+	int nthr;
+	struct wf_worker w[WF_MAX_THREADS];
 	struct wf_job jobs[WF_QUEUE];
-	uint32_t head;      /* next job to issue (I/O thread) */
-	uint32_t tail;      /* next free slot (submit) */
-	uint32_t reported;  /* next job to report (poll) */
-	pthread_t thr;
-	int thr_started;
+	uint32_t tail;                  /* next free slot (submit) */
+	uint32_t reported;              /* next job to report (poll) */
 	pthread_mutex_t mu;
 	pthread_cond_t cv;
 	int stop;
@@ -121,85 +143,148 @@ static void set_error(struct kllm_wavefront_ctx *c)
 	pthread_mutex_unlock(&c->mu);
 }
 
-static void issue(struct kllm_wavefront_ctx *c, struct wf_job *j)
+static uint64_t round16(uint64_t x)
 {
-	for (uint32_t i = 0; i < j->n; i++) {
+	return (x + 15u) & ~(uint64_t)15u;
+}
+
+/* Copies chunk b (`used` bytes) to the device and places its records. */
+static int flush(struct kllm_wavefront_ctx *c, struct wf_worker *wk, int b,
+		 const struct kllm_wf_scatter *s, uint64_t used)
+{
+	if (cudaMemcpyAsync(wk->dev_stage[b], wk->stage[b], used, cudaMemcpyHostToDevice,
+			    wk->stream) != cudaSuccess ||
+	    kllm_wf_scatter_launch(s, wk->dev_stage[b], wk->stream) != 0 ||
+	    cudaEventRecord(wk->stage_ev[b], wk->stream) != cudaSuccess) {
+		cudaGetLastError();
+		set_error(c);
+		return -1;
+	}
+	return 0;
+}
+
+/* This thread's share of one job: blocks id, id + threads, ... */
+static void issue(struct kllm_wavefront_ctx *c, struct wf_worker *wk, struct wf_job *j)
+{
+	uint32_t failed = 0;
+	uint64_t bytes = 0, chunk_sum = 0, used = 0;
+	struct kllm_wf_scatter s;
+	int b = -1;                             /* chunk being filled */
+	s.n = 0;
+	s.reserved = 0;
+	for (uint32_t i = (uint32_t)wk->id; i < j->n; i += (uint32_t)c->nthr) {
 		struct wf_item *it = &j->items[i];
 		if (!it->ok)
 			continue;
-		const int b = c->stage_next;
-		c->stage_next = (b + 1) % c->n_stage;
-		/* the buffer's previous copy must have left it */
-		if (cudaEventSynchronize(c->stage_ev[b]) != cudaSuccess) {
-			set_error(c);
-			it->ok = 0;
-			j->failed++;
+		if (b >= 0 && used + round16(it->bytes) > c->chunk_bytes) {
+			if (flush(c, wk, b, &s, used))
+				failed += s.n;
+			else
+				bytes += chunk_sum;
+			b = -1;
+		}
+		if (b < 0) {
+			b = wk->next;
+			wk->next = (b + 1) % wk->n_stage;
+			/* the chunk's previous scatter must have finished with it */
+			if (cudaEventSynchronize(wk->stage_ev[b]) != cudaSuccess) {
+				cudaGetLastError();
+				set_error(c);
+				failed++;
+				b = -1;
+				continue;
+			}
+			s.n = 0;
+			used = chunk_sum = 0;
+		}
+		if (read_full(c->fd, wk->stage[b] + used, it->bytes, it->off)) {
+			failed++;
 			continue;
 		}
-		if (read_full(c->fd, c->stage[b], it->bytes, it->off)) {
-			it->ok = 0;
-			j->failed++;
-			continue;
-		}
-		if (cudaMemcpyAsync((void *)(uintptr_t)it->dst, c->stage[b], it->bytes,
-				    cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
-		    cudaEventRecord(c->stage_ev[b], c->stream) != cudaSuccess) {
-			set_error(c);
-			it->ok = 0;
-			j->failed++;
-			continue;
-		}
-		j->bytes += it->bytes;
+		s.dst[s.n] = it->dst;
+		s.bytes[s.n] = it->bytes;
+		s.off[s.n] = (uint32_t)used;
+		s.n++;
+		used += round16(it->bytes);
+		chunk_sum += it->bytes;
 	}
-	if (cudaEventRecord(j->done, c->stream) != cudaSuccess)
+	if (b >= 0 && s.n) {
+		if (flush(c, wk, b, &s, used))
+			failed += s.n;
+		else
+			bytes += chunk_sum;
+	}
+	__atomic_add_fetch(&j->failed, failed, __ATOMIC_RELAXED);
+	__atomic_add_fetch(&j->bytes, bytes, __ATOMIC_RELAXED);
+	if (cudaEventRecord(j->done[wk->id], wk->stream) != cudaSuccess)
 		set_error(c);
 }
 
 static void *io_main(void *arg)
 {
-	struct kllm_wavefront_ctx *c = arg;
+	struct wf_worker *wk = arg;
+	struct kllm_wavefront_ctx *c = wk->c;
 	cudaSetDevice(c->device);
 	pthread_mutex_lock(&c->mu);
 	for (;;) {
-		while (!c->stop && c->head == c->tail)
+		while (!c->stop && wk->head == c->tail)
 			pthread_cond_wait(&c->cv, &c->mu);
-		if (c->head == c->tail && c->stop)
+		if (wk->head == c->tail && c->stop)
 			break;
-		struct wf_job *j = &c->jobs[c->head % WF_QUEUE];
+		struct wf_job *j = &c->jobs[wk->head % WF_QUEUE];
 		pthread_mutex_unlock(&c->mu);
-		issue(c, j);
+		issue(c, wk, j);
 		pthread_mutex_lock(&c->mu);
-		j->state = JOB_ISSUED;
-		c->head++;
+		wk->head++;                     /* the mutex publishes this thread's counts */
 	}
 	pthread_mutex_unlock(&c->mu);
 	return NULL;
+}
+
+/* Every thread has issued job `idx` (caller holds mu). */
+static int issued_by_all(const struct kllm_wavefront_ctx *c, uint32_t idx)
+{
+	for (int t = 0; t < c->nthr; t++)
+		if ((int32_t)(c->w[t].head - idx) <= 0)
+			return 0;
+	return 1;
 }
 
 void kllm_wavefront_destroy(struct kllm_wavefront_ctx *c)
 {
 	if (!c)
 		return;
-	if (c->thr_started) {
-		pthread_mutex_lock(&c->mu);
-		c->stop = 1;
-		pthread_cond_signal(&c->cv);
-		pthread_mutex_unlock(&c->mu);
-		pthread_join(c->thr, NULL);
-	}
-	if (c->stream)
-		cudaStreamSynchronize(c->stream);
-	for (int b = 0; b < c->n_stage; b++) {
-		if (c->stage[b])
-			cudaFreeHost(c->stage[b]);
-		if (c->stage_ev[b])
-			cudaEventDestroy(c->stage_ev[b]);
+	pthread_mutex_lock(&c->mu);
+	c->stop = 1;
+	pthread_cond_broadcast(&c->cv);
+	pthread_mutex_unlock(&c->mu);
+	for (int t = 0; t < c->nthr; t++)
+		if (c->w[t].started)
+			pthread_join(c->w[t].thr, NULL);
+	int prev = -1;
+	const int switched = c->nthr > 0 && cudaGetDevice(&prev) == cudaSuccess &&
+			     cudaSetDevice(c->device) == cudaSuccess;
+	for (int t = 0; t < c->nthr; t++) {
+		struct wf_worker *wk = &c->w[t];
+		if (wk->stream)
+			cudaStreamSynchronize(wk->stream);
+		for (int b = 0; b < wk->n_stage; b++) {
+			if (wk->stage[b])
+				cudaFreeHost(wk->stage[b]);
+			if (wk->dev_stage[b])
+				cudaFree(wk->dev_stage[b]);
+			if (wk->stage_ev[b])
+				cudaEventDestroy(wk->stage_ev[b]);
+		}
+		if (wk->stream)
+			cudaStreamDestroy(wk->stream);
 	}
 	for (int i = 0; i < WF_QUEUE; i++)
-		if (c->jobs[i].done)
-			cudaEventDestroy(c->jobs[i].done);
-	if (c->stream)
-		cudaStreamDestroy(c->stream);
+		for (int t = 0; t < WF_MAX_THREADS; t++)
+			if (c->jobs[i].done[t])
+				cudaEventDestroy(c->jobs[i].done[t]);
+	if (switched)
+		cudaSetDevice(prev);
 	if (c->fd >= 0)
 		close(c->fd);
 	pthread_cond_destroy(&c->cv);
@@ -210,8 +295,8 @@ void kllm_wavefront_destroy(struct kllm_wavefront_ctx *c)
 struct kllm_wavefront_ctx *kllm_wavefront_create2(const char *store_path, int device,
 						  uint64_t max_block_bytes, int staging_buffers)
 {
-	if (!store_path || device < 0 || max_block_bytes == 0 || staging_buffers < 2 ||
-	    staging_buffers > 64)
+	if (!store_path || device < 0 || max_block_bytes == 0 ||
+	    max_block_bytes > (1ull << 30) || staging_buffers < 2 || staging_buffers > 64)
 		return NULL;
 	struct kllm_wavefront_ctx *c = calloc(1, sizeof(*c));
 	if (!c)
@@ -220,38 +305,61 @@ struct kllm_wavefront_ctx *kllm_wavefront_create2(const char *store_path, int de
 	pthread_mutex_init(&c->mu, NULL);
 	pthread_cond_init(&c->cv, NULL);
 	c->device = device;
-	c->n_stage = staging_buffers;
 	c->stage_bytes = max_block_bytes;
+	c->chunk_bytes = round16(max_block_bytes) > WF_MIN_CHUNK ? round16(max_block_bytes)
+								 : WF_MIN_CHUNK;
+	/* two or more staging chunks per thread, at most four threads */
+	c->nthr = staging_buffers / 2 < WF_MAX_THREADS ? staging_buffers / 2 : WF_MAX_THREADS;
+	const int per = staging_buffers / c->nthr < WF_MAX_STAGE ? staging_buffers / c->nthr
+								 : WF_MAX_STAGE;
 	c->fd = open(store_path, O_RDONLY | O_CLOEXEC);
 	int ndev = 0, prev = -1;
 	if (c->fd < 0 || cudaGetDeviceCount(&ndev) != cudaSuccess || device >= ndev ||
-	    cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(device) != cudaSuccess)
-		goto fail;
+	    cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(device) != cudaSuccess) {
+		cudaGetLastError();
+		c->nthr = 0;
+		kllm_wavefront_destroy(c);
+		return NULL;
+	}
 	/* the caller's current device is put back before returning */
-	const cudaError_t se = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-	if (se != cudaSuccess)
+	void *fn = NULL;
+	enum cudaDriverEntryPointQueryResult q;
+	if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) !=
+		cudaSuccess ||
+	    q != cudaDriverEntryPointSuccess || !fn)
 		goto fail_dev;
-	for (int b = 0; b < c->n_stage; b++)
-		if (cudaHostAlloc((void **)&c->stage[b], max_block_bytes, cudaHostAllocDefault) !=
-			cudaSuccess ||
-		    cudaEventCreateWithFlags(&c->stage_ev[b], cudaEventDisableTiming) != cudaSuccess)
+	c->get_range = (CUresult(*)(CUdeviceptr *, size_t *, CUdeviceptr))fn;
+	for (int t = 0; t < c->nthr; t++) {
+		struct wf_worker *wk = &c->w[t];
+		wk->c = c;
+		wk->id = t;
+		wk->n_stage = per;
+		if (cudaStreamCreateWithFlags(&wk->stream, cudaStreamNonBlocking) != cudaSuccess)
 			goto fail_dev;
+		for (int b = 0; b < per; b++)
+			if (cudaHostAlloc((void **)&wk->stage[b], c->chunk_bytes,
+					  cudaHostAllocDefault) != cudaSuccess ||
+			    cudaMalloc((void **)&wk->dev_stage[b], c->chunk_bytes) != cudaSuccess ||
+			    cudaEventCreateWithFlags(&wk->stage_ev[b], cudaEventDisableTiming) !=
+				cudaSuccess)
+				goto fail_dev;
+	}
 	for (int i = 0; i < WF_QUEUE; i++)
-		if (cudaEventCreateWithFlags(&c->jobs[i].done, cudaEventDisableTiming) != cudaSuccess)
+		for (int t = 0; t < c->nthr; t++)
+			if (cudaEventCreateWithFlags(&c->jobs[i].done[t], cudaEventDisableTiming) !=
+			    cudaSuccess)
+				goto fail_dev;
+	for (int t = 0; t < c->nthr; t++) {
+		if (pthread_create(&c->w[t].thr, NULL, io_main, &c->w[t]))
 			goto fail_dev;
-	if (pthread_create(&c->thr, NULL, io_main, c))
-		goto fail_dev;
-	c->thr_started = 1;
+		c->w[t].started = 1;
+	}
 	cudaSetDevice(prev);
 	return c;
 fail_dev:
 	kllm_wavefront_destroy(c);
 	cudaSetDevice(prev);
 	cudaGetLastError();
-	return NULL;
-fail:
-	cudaGetLastError();
-	kllm_wavefront_destroy(c);
 	return NULL;
 }
 
@@ -274,6 +382,49 @@ int kllm_wavefront_set_index(struct kllm_wavefront_ctx *c,
 	return KLLM_OK;
 }
 
+struct wf_range {
+	uint64_t lo, hi;
+};
+
+/* [dst, dst + bytes) lies inside one allocation of device memory on this
+ * context's GPU. `seen` remembers the allocations found during one submit. */
+static int dest_ok(struct kllm_wavefront_ctx *c, uint64_t dst, uint64_t bytes,
+		   struct wf_range *seen, int *n_seen)
+{
+	const uint64_t end = dst + bytes;
+	if (!dst || end < dst)
+		return 0;
+	for (int r = 0; r < *n_seen; r++)
+		if (dst >= seen[r].lo && end <= seen[r].hi)
+			return 1;
+	struct cudaPointerAttributes a;
+	memset(&a, 0, sizeof(a));
+	if (cudaPointerGetAttributes(&a, (const void *)(uintptr_t)dst) != cudaSuccess) {
+		cudaGetLastError();
+		return 0;
+	}
+	if ((a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) ||
+	    a.device != c->device)
+		return 0;
+	int prev = -1;
+	CUdeviceptr base = 0;
+	size_t size = 0;
+	if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(c->device) != cudaSuccess) {
+		cudaGetLastError();
+		return 0;
+	}
+	const CUresult r = c->get_range(&base, &size, (CUdeviceptr)dst);
+	cudaSetDevice(prev);
+	if (r != CUDA_SUCCESS || dst < (uint64_t)base || end > (uint64_t)base + size)
+		return 0;
+	if (*n_seen < WF_RANGES) {
+		seen[*n_seen].lo = (uint64_t)base;
+		seen[*n_seen].hi = (uint64_t)base + size;
+		(*n_seen)++;
+	}
+	return 1;
+}
+
 int kllm_wavefront_submit(struct kllm_wavefront_ctx *c, const struct kllm_wavefront *wf)
 {
 	if (!c || !wf || wf->num_blocks == 0 || wf->num_blocks > KLLM_WAVEFRONT_MAX_BLOCKS ||
@@ -287,6 +438,8 @@ int kllm_wavefront_submit(struct kllm_wavefront_ctx *c, const struct kllm_wavefr
 	j->n = wf->num_blocks;
 	j->failed = 0;
 	j->bytes = 0;
+	struct wf_range seen[WF_RANGES];
+	int n_seen = 0;
 	for (uint32_t i = 0; i < j->n; i++) {
 		const struct kllm_wf_block_desc *d = &wf->blocks[i];
 		struct wf_item *it = &j->items[i];
@@ -295,14 +448,14 @@ int kllm_wavefront_submit(struct kllm_wavefront_ctx *c, const struct kllm_wavefr
 		it->bytes = d->block_size;
 		it->off = c->base_offset + (uint64_t)(rec < 0 ? 0 : rec) * c->record_bytes;
 		it->ok = rec >= 0 && d->block_size > 0 && d->block_size <= c->stage_bytes &&
-			 d->block_size <= c->record_bytes && d->vram_dest_addr;
+			 d->block_size <= c->record_bytes &&
+			 dest_ok(c, d->vram_dest_addr, d->block_size, seen, &n_seen);
 		if (!it->ok)
 			j->failed++;
 	}
 	pthread_mutex_lock(&c->mu);
-	j->state = JOB_QUEUED;
 	c->tail++;
-	pthread_cond_signal(&c->cv);
+	pthread_cond_broadcast(&c->cv);
 	pthread_mutex_unlock(&c->mu);
 	return 0;
 }
@@ -315,18 +468,23 @@ int kllm_wavefront_poll(struct kllm_wavefront_ctx *c, struct kllm_wf_completion 
 	int n = 0;
 	while (n < max_completions) {
 		pthread_mutex_lock(&c->mu);
-		const int issued = c->reported != c->head;
+		const int issued = c->reported != c->tail && issued_by_all(c, c->reported);
 		pthread_mutex_unlock(&c->mu);
 		if (!issued)
 			break;
 		struct wf_job *j = &c->jobs[c->reported % WF_QUEUE];
-		const cudaError_t q = cudaEventQuery(j->done);
-		if (q == cudaErrorNotReady)
-			break;
-		if (q != cudaSuccess) {
-			cudaGetLastError();
-			set_error(c);
+		int busy = 0;
+		for (int t = 0; t < c->nthr && !busy; t++) {
+			const cudaError_t q = cudaEventQuery(j->done[t]);
+			if (q == cudaErrorNotReady) {
+				busy = 1;
+			} else if (q != cudaSuccess) {
+				cudaGetLastError();
+				set_error(c);
+			}
 		}
+		if (busy)
+			break;
 		out[n].sequence_id = j->seq;
 		out[n].blocks_failed = j->failed;
 		out[n].blocks_completed = j->n - j->failed;
@@ -334,7 +492,6 @@ int kllm_wavefront_poll(struct kllm_wavefront_ctx *c, struct kllm_wf_completion 
 		out[n].latency_ns = mono_ns() - j->t0;
 		n++;
 		pthread_mutex_lock(&c->mu);
-		j->state = JOB_FREE;
 		c->reported++;
 		pthread_mutex_unlock(&c->mu);
 	}
