@@ -102,33 +102,14 @@ __device__ __forceinline__ uint32_t mx_scale_code_tab(float amax, const float *t
 	return c == 0u ? 1u : c;
 }
 
-// Writes micro-block x (b of kv head h, K or V) to position pos of sequence
-// seq: bf16 copy, MX-FP8 quantization, or the reference's BF16-payload form.
+// Writes micro-block x (b of its kv head, K or V) at `slot` of the kv
+// head's section `sec`: bf16 copy, MX-FP8 quantization, or the reference's
+// BF16-payload form.
 __device__ __forceinline__ void append_store(const kllm_append_args &a, const float *tab,
-					     uint4 x, int seq, int pos, int h, int kv, int b)
+					     uint4 x, uint8_t *sec, int slot, int b)
 {
 	const int bs = a.block_size;
-	const bool pow2 = (bs & (bs - 1)) == 0;
-	const int lg = __ffs(bs) - 1;
-	const int blk = pos >= 0 ? (pow2 ? pos >> lg : pos / bs) : -1;
-	if (seq < 0 || seq >= a.num_seqs || blk < 0 || blk >= a.max_blocks) {
-		if (a.err && b == 0)
-			atomicOr(a.err, 0x4u);
-		return;
-	}
-	const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
-			    (size_t)seq * a.max_blocks + blk;
-	const unsigned long long base = kv ? e->v : e->k;
-	if (!e->valid || !e->k || !base) {
-		if (a.err && b == 0)
-			atomicOr(a.err, 0x4u);
-		return;
-	}
-	const int slot = pos - blk * bs;
 	const int d = a.head_dim;
-	uint8_t *sec = reinterpret_cast<uint8_t *>(base) + a.layer_off +
-		       (size_t)h * section_bytes(a.kv_dtype, bs, d);
-
 	if (a.kv_dtype == 0) {
 		*reinterpret_cast<uint4 *>(sec + ((size_t)slot * d + b * 8) * 2) = x;
 		return;
@@ -192,14 +173,54 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, const fl
 
 // Grid x = groups of kTokensPerCta tokens, y = 256-thread slices of a
 // token's 2 x num_kv_heads x head_dim/8 micro-blocks (K first, then V); one
-// thread per micro-block and token. Every thread first issues the data loads
-// of all its tokens, then resolves their pages, so several independent loads
-// are in flight per thread and a warp reads 512 contiguous bytes per token.
+// thread per micro-block and token. The first threads resolve each token's
+// page once for the CTA (block-table entry -> K and V section base, slot);
+// every thread issues the data loads of all its tokens before it writes, so
+// several independent loads are in flight per thread and a warp reads 512
+// contiguous bytes per token.
 constexpr int kTokensPerCta = 4;
 
-__device__ __forceinline__ void append_tokens(const kllm_append_args &a, const float *tab,
-					      int i0, const int *seqs, const int *poss)
+// Page of token t (sequence seq, position pos) for K (kv 0) or V: the
+// address of kv head 0's section in the page, or 0 when the token has no
+// page (flagged in err, as every write of that token is dropped).
+__device__ __forceinline__ unsigned long long append_page(const kllm_append_args &a, int seq,
+							  int pos, int kv, int &slot)
 {
+	const int bs = a.block_size;
+	const bool pow2 = (bs & (bs - 1)) == 0;
+	const int lg = __ffs(bs) - 1;
+	const int blk = pos >= 0 ? (pow2 ? pos >> lg : pos / bs) : -1;
+	slot = 0;
+	if (seq < 0 || seq >= a.num_seqs || blk < 0 || blk >= a.max_blocks)
+		return 0ull;
+	const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+			    (size_t)seq * a.max_blocks + blk;
+	const unsigned long long base = kv ? e->v : e->k;
+	if (!e->valid || !e->k || !base)
+		return 0ull;
+	slot = pos - blk * bs;
+	return base + a.layer_off;
+}
+
+// seqs/poss: the CTA's tokens (shared memory, filled before the call).
+__device__ __forceinline__ void append_tokens(const kllm_append_args &a, const float *tab, int i0,
+					      const int *seqs, const int *poss)
+{
+	__shared__ unsigned long long s_page[kTokensPerCta][2];
+	__shared__ int s_slot[kTokensPerCta][2];
+	if (threadIdx.x < 2 * kTokensPerCta) {
+		const int t = threadIdx.x >> 1, kv = threadIdx.x & 1;
+		int slot = 0;
+		unsigned long long page = 0ull;
+		if (i0 + t < a.num_tokens) {
+			page = append_page(a, seqs[t], poss[t], kv, slot);
+			if (!page && a.err)
+				atomicOr(a.err, 0x4u);
+		}
+		s_page[t][kv] = page;
+		s_slot[t][kv] = slot;
+	}
+	__syncthreads();
 	const int nb = a.head_dim >> 3;
 	const int per_kv = a.num_kv_heads * nb;
 	const int u = blockIdx.y * blockDim.x + threadIdx.x;
@@ -208,29 +229,34 @@ __device__ __forceinline__ void append_tokens(const kllm_append_args &a, const f
 	const int kv = u >= per_kv ? 1 : 0;
 	const int rem = u - kv * per_kv;
 	const int h = rem / nb, b = rem - h * nb;
+	const size_t hoff = (size_t)h * section_bytes(a.kv_dtype, a.block_size, a.head_dim);
 	uint4 x[kTokensPerCta];
 #pragma unroll
 	for (int t = 0; t < kTokensPerCta; ++t)
 		if (i0 + t < a.num_tokens)
 			x[t] = append_load(a, i0 + t, h, kv, b);
 #pragma unroll
-	for (int t = 0; t < kTokensPerCta; ++t)
-		if (i0 + t < a.num_tokens)
-			append_store(a, tab, x[t], seqs[t], poss[t], h, kv, b);
+	for (int t = 0; t < kTokensPerCta; ++t) {
+		const unsigned long long page = s_page[t][kv];
+		if (i0 + t < a.num_tokens && page)
+			append_store(a, tab, x[t], reinterpret_cast<uint8_t *>(page) + hoff,
+				     s_slot[t][kv], b);
+	}
 }
 
 __global__ void __launch_bounds__(256) append_kernel(const kllm_append_args a)
 {
+	__shared__ int s_seq[kTokensPerCta], s_pos[kTokensPerCta];
 	const float *tab = g_e4m3.v;
 	const int i0 = blockIdx.x * kTokensPerCta;
-	int seqs[kTokensPerCta], poss[kTokensPerCta];
-#pragma unroll
-	for (int t = 0; t < kTokensPerCta; ++t) {
-		const bool in = i0 + t < a.num_tokens;
-		seqs[t] = in ? a.token_seq[i0 + t] : -1;
-		poss[t] = in ? a.token_pos[i0 + t] : -1;
+	if (threadIdx.x < kTokensPerCta) {
+		const int i = i0 + threadIdx.x;
+		const bool in = i < a.num_tokens;
+		s_seq[threadIdx.x] = in ? a.token_seq[i] : -1;
+		s_pos[threadIdx.x] = in ? a.token_pos[i] : -1;
 	}
-	append_tokens(a, tab, i0, seqs, poss);
+	__syncthreads();
+	append_tokens(a, tab, i0, s_seq, s_pos);
 }
 
 // Same, with the (sequence, position) of row i derived from chunk offsets.

@@ -69,7 +69,9 @@ struct PrefillSmem {
 	// S(j) are done, V(j) (and the key mask, read by the softmax of block j)
 	// once both PV(j) are issued after the softmax
 	uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-	uint64_t s_full[2], p_full[2], o_full[2];
+	// p_half: P of keys 0-63 written (the PV of that half may start while
+	// the softmax finishes keys 64-127); p_full: all of P written
+	uint64_t s_full[2], p_half[2], p_full[2], o_full[2];
 	uint64_t drain;
 	uint32_t tmem_base;
 	int abort;
@@ -296,11 +298,12 @@ __device__ __forceinline__ void tmem_wait_ld_row(uint32_t (&r)[8][16])
 // p = 2^pexp x exp2(s x sl2 - m_ref); l_sum gains sum(p) / 2^pexp. Invalid
 // keys are set to -inf first (p = 0). The row's block max is known before
 // any P is written, so raising the reference max rescales only O and l.
-// o_live: O already holds earlier blocks. Branches around TMEM accesses are
-// warp-uniform.
+// o_live: O already holds earlier blocks. Once keys 0-63 are written the
+// thread arrives on p_half, so that half of the PV product can start.
+// Branches around TMEM accesses are warp-uniform.
 __device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const uint32_t (&vmask)[4],
 					      bool masked, float sl2, float pexp, bool o_live,
-					      float &m_ref, float &l_sum)
+					      float &m_ref, float &l_sum, uint64_t *p_half)
 {
 	uint32_t r[8][16];
 #pragma unroll
@@ -349,6 +352,11 @@ __device__ __forceinline__ void softmax_block(uint32_t tS, uint32_t tO, const ui
 			pack_p_pair(q0, q1, w[i], w[8 + i]);
 		}
 		tmem_st16_nowait(tS + 16 * g, w);
+		if (g == 3) {
+			tmem_wait_st();
+			tc_fence_before();
+			mbar_arrive(p_half);
+		}
 	}
 	tmem_wait_st();
 	l_sum += bsum * exp2f(-pexp);
@@ -393,6 +401,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 		}
 		for (int t = 0; t < 2; ++t) {
 			mbar_init(&sm.s_full[t], 1);
+			mbar_init(&sm.p_half[t], 128);
 			mbar_init(&sm.p_full[t], 128);
 			mbar_init(&sm.o_full[t], 1);
 		}
@@ -461,7 +470,7 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			const float pexp = prior && a.kv_dtype == 1 ? 8.f : 0.f;
 			const bool full = __all_sync(0xffffffffu, (vmask[0] & vmask[1] & vmask[2] &
 								   vmask[3]) == 0xFFFFFFFFu);
-			softmax_block(tS, tO, vmask, !full, sl2, pexp, j > 0, m_ref, l_sum);
+			softmax_block(tS, tO, vmask, !full, sl2, pexp, j > 0, m_ref, l_sum, &sm.p_half[t]);
 			tc_fence_before();
 			mbar_arrive(&sm.p_full[t]);
 		}
@@ -638,11 +647,12 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			}
 			__syncwarp();
 		};
-		auto issue_pv = [&](int t, int st, bool first) {
+		// half 0: keys 0-63 (P groups 0-3), half 1: keys 64-127
+		auto issue_pv = [&](int t, int st, bool first, int half) {
 			const uint64_t dv = st ? dv1 : dv0;
 			const uint32_t d = tmem + col_o(t), pa = tmem + col_s(t);
 #pragma unroll
-			for (int kk = 0; kk < 2 * kKeys / 16; ++kk) {
+			for (int kk = half * kKeys / 16; kk < (half + 1) * kKeys / 16; ++kk) {
 				const int g = kk >> 1;     // 16-key group; kk odd: the lo half of P
 				if (leader)
 					umma_f16_ts(d, pa + 16u * g + 8u * (kk & 1), dv + (uint64_t)((g * 2048) >> 4),
@@ -675,12 +685,18 @@ prefill_kernel(const kllm_prefill_args a, const __grid_constant__ CUtensorMap tm
 			ok = wait_all(&sm.v_full[st], (uint32_t)((j / kStages) & 1));
 			for (int t = 0; t < 2 && ok; ++t) {
 				if (j < nb_t[t]) {
+					if (!wait_all(&sm.p_half[t], (uint32_t)(j & 1))) {
+						ok = false;
+						break;
+					}
+					tc_fence_after();
+					issue_pv(t, st, j == 0, 0);
 					if (!wait_all(&sm.p_full[t], (uint32_t)(j & 1))) {
 						ok = false;
 						break;
 					}
 					tc_fence_after();
-					issue_pv(t, st, j == 0);
+					issue_pv(t, st, j == 0, 1);
 				}
 				if (t == 1)
 					commit(&sm.v_empty[st]);   // both PV(j) issued: V(j) free when done
