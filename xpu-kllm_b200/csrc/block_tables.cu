@@ -17,15 +17,15 @@
 // tokens is one 64-byte SHA-256 message block, so the running hash state
 // after j message blocks (a "midstate") serves every table block whose
 // prefix ends in message block j. Two kernels:
-//   chain_kernel     one thread per sequence runs the sequential
-//                    compressions over the sequence's full message blocks
-//                    and stores every midstate (32 B) in the workspace; its
-//                    tokens arrive through a per-lane shared-memory ring
-//                    (cp.async, three message blocks ahead), so the chain
-//                    never waits on global memory. The chain itself is
-//                    latency-bound: one compression is 64 dependent rounds
-//                    (about 35 cycles each on sm_100: a funnel-shift rotate,
-//                    a three-way xor and a three-way add per critical step);
+//   chain_kernel     32 sequences per CTA, two warps. The message schedule
+//                    depends only on the tokens, so warp 1 expands each
+//                    message block into W[t] + K[t] (t = 0..63) in a
+//                    shared-memory ring four blocks deep, and warp 0 runs
+//                    only the 64 dependent rounds per block (a funnel-shift
+//                    rotate, a three-way xor and a three-way add per
+//                    critical step) and stores every midstate (32 B) in the
+//                    workspace. The chain is latency-bound: the longest
+//                    sequence's compressions run one after another;
 //   finalize_kernel  one thread per (sequence, table block): the tail tokens
 //                    and the FIPS 180-4 padding on top of the right midstate
 //                    (one or two compressions), the index probe, the LRU
@@ -121,27 +121,58 @@ __device__ __forceinline__ uint32_t *midstate(const kllm_table_args &a, int s, i
 	return a.midstates + ((size_t)s * a.ms_stride + j) * 8;
 }
 
-constexpr int kChainThreads = 64;
-constexpr int kDepth = 4;                       // message blocks in flight per lane
-constexpr int kLaneWords = kDepth * 16 + 4;     // +4: conflict-free 16-byte reads
-
-__device__ __forceinline__ void cp_async4(uint32_t *dst, const uint32_t *src)
+// FIPS 180-4 6.2.2 step 4 alone: the 64 rounds over a precomputed schedule,
+// wk[t * stride] = W[t] + K[t].
+__device__ __forceinline__ void sha_rounds(uint32_t (&h)[8], const uint32_t *wk, int stride)
 {
-	asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::
-		     "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+	uint32_t a = h[0], b = h[1], c = h[2], d = h[3];
+	uint32_t e = h[4], f = h[5], g = h[6], hh = h[7];
+#pragma unroll
+	for (int t = 0; t < 64; ++t) {
+		const uint32_t t1 = hh + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) +
+				    ((e & f) ^ (~e & g)) + wk[t * stride];
+		const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) +
+				    ((a & b) ^ (a & c) ^ (b & c));
+		hh = g;
+		g = f;
+		f = e;
+		e = d + t1;
+		d = c;
+		c = b;
+		b = a;
+		a = t1 + t2;
+	}
+	h[0] += a; h[1] += b; h[2] += c; h[3] += d;
+	h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
 }
 
-__global__ void __launch_bounds__(kChainThreads) chain_kernel(const kllm_table_args a)
+constexpr int kChainLanes = 32;     // sequences per CTA: warp 0 chains, warp 1 schedules
+constexpr int kSlots = 4;           // message blocks in flight between the two warps
+// Named barriers (64 threads: both warps), ids 1..kSlots: slot written by
+// warp 1; ids kSlots+1..2*kSlots: slot read by warp 0. Both warps run the
+// same warp-uniform number of iterations, so every barrier instance gets
+// its 64 arrivals.
+__device__ __forceinline__ void bar_sync64(int id)
 {
-	__shared__ __align__(16) uint32_t ring[kChainThreads * kLaneWords];
-	const int s = blockIdx.x * blockDim.x + threadIdx.x;
-	if (s == 0 && a.miss_count)
+	asm volatile("bar.sync %0, 64;" :: "r"(id) : "memory");
+}
+__device__ __forceinline__ void bar_arrive64(int id)
+{
+	asm volatile("bar.arrive %0, 64;" :: "r"(id) : "memory");
+}
+
+__global__ void __launch_bounds__(2 * kChainLanes) chain_kernel(const kllm_table_args a)
+{
+	__shared__ uint32_t wk[kSlots][64][kChainLanes];    // lane-minor: conflict-free
+	const int lane = threadIdx.x & 31, role = threadIdx.x >> 5;
+	const int s = blockIdx.x * kChainLanes + lane;
+	if (blockIdx.x == 0 && threadIdx.x == 0 && a.miss_count)
 		*a.miss_count = 0;
 	int full = 0, j0 = 0;
 	const uint32_t *tok = a.tokens;
 	if (s < a.num_seqs) {
 		const int raw = a.seq_lens[s];
-		if ((long long)raw > (long long)a.max_blocks * a.block_size && a.err)
+		if (role == 0 && (long long)raw > (long long)a.max_blocks * a.block_size && a.err)
 			atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
 		const int len = tabled_len(a, s);
 		const int b0 = a.first_block ? max(a.first_block[s], 0) : 0;
@@ -149,11 +180,54 @@ __global__ void __launch_bounds__(kChainThreads) chain_kernel(const kllm_table_a
 		j0 = (int)(((long long)b0 * a.block_size) >> 4);
 		tok = a.tokens + a.starts[s];
 	}
-	if (j0 >= full)
+	// this lane's message blocks j0 .. full - 1; the warp runs the longest
+	const int mine = max(full - j0, 0);
+	const int n = __reduce_max_sync(0xffffffffu, mine);
+	if (n == 0)
+		return;                     // the other warp sees the same n
+	if (role == 1) {
+		// ---- schedule: tokens -> W[t] + K[t], one block ahead in registers
+		uint32_t nxt[16];
+#pragma unroll
+		for (int k = 0; k < 16; ++k)
+			nxt[k] = mine > 0 ? tok[(size_t)j0 * 16 + k] : 0u;
+		for (int i = 0; i < n; ++i) {
+			const int slot = i % kSlots;
+			uint32_t w[16];
+#pragma unroll
+			for (int k = 0; k < 16; ++k)
+				w[k] = msg_word(nxt[k]);
+			if (i + 1 < mine) {
+#pragma unroll
+				for (int k = 0; k < 16; ++k)
+					nxt[k] = tok[(size_t)(j0 + i + 1) * 16 + k];
+			}
+			if (i >= kSlots)
+				bar_sync64(1 + kSlots + slot);     // warp 0 is done with block i - kSlots
+			if (i < mine) {
+#pragma unroll
+				for (int t = 0; t < 64; ++t) {
+					uint32_t wt;
+					if (t < 16) {
+						wt = w[t];
+					} else {
+						const uint32_t x15 = w[(t - 15) & 15], x2 = w[(t - 2) & 15];
+						const uint32_t s0 = rotr(x15, 7) ^ rotr(x15, 18) ^ (x15 >> 3);
+						const uint32_t s1 = rotr(x2, 17) ^ rotr(x2, 19) ^ (x2 >> 10);
+						wt = w[t & 15] + s0 + w[(t - 7) & 15] + s1;
+						w[t & 15] = wt;
+					}
+					wk[slot][t][lane] = wt + kShaK[t];
+				}
+			}
+			__threadfence_block();
+			bar_arrive64(1 + slot);
+		}
 		return;
-	uint32_t *mine = ring + threadIdx.x * kLaneWords;
+	}
+	// ---- chain: 64 rounds per block over the ring, midstate after each
 	uint32_t h[8];
-	if (j0 == 0) {
+	if (j0 == 0 || mine == 0) {
 		sha_iv(h);
 	} else {
 		const uint4 *m = reinterpret_cast<const uint4 *>(midstate(a, s, j0));
@@ -161,40 +235,18 @@ __global__ void __launch_bounds__(kChainThreads) chain_kernel(const kllm_table_a
 		h[0] = lo.x; h[1] = lo.y; h[2] = lo.z; h[3] = lo.w;
 		h[4] = hi.x; h[5] = hi.y; h[6] = hi.z; h[7] = hi.w;
 	}
-#pragma unroll
-	for (int d = 0; d < kDepth - 1; ++d) {
-		if (j0 + d < full) {
-#pragma unroll
-			for (int k = 0; k < 16; ++k)
-				cp_async4(mine + ((j0 + d) % kDepth) * 16 + k, tok + (size_t)(j0 + d) * 16 + k);
+	for (int i = 0; i < n; ++i) {
+		const int slot = i % kSlots;
+		bar_sync64(1 + slot);
+		if (i < mine) {
+			sha_rounds(h, &wk[slot][0][lane], kChainLanes);
+			uint4 *m = reinterpret_cast<uint4 *>(midstate(a, s, j0 + i + 1));
+			m[0] = make_uint4(h[0], h[1], h[2], h[3]);
+			m[1] = make_uint4(h[4], h[5], h[6], h[7]);
 		}
-		asm volatile("cp.async.commit_group;" ::: "memory");
+		if (i + kSlots < n)
+			bar_arrive64(1 + kSlots + slot);   // warp 1 refills this slot next
 	}
-	for (int j = j0; j < full; ++j) {
-		const int jn = j + kDepth - 1;
-		if (jn < full) {
-#pragma unroll
-			for (int k = 0; k < 16; ++k)
-				cp_async4(mine + (jn % kDepth) * 16 + k, tok + (size_t)jn * 16 + k);
-		}
-		asm volatile("cp.async.commit_group;" ::: "memory");
-		asm volatile("cp.async.wait_group %0;" :: "n"(kDepth - 1) : "memory");
-		const uint4 *src = reinterpret_cast<const uint4 *>(mine + (j % kDepth) * 16);
-		uint32_t w[16];
-#pragma unroll
-		for (int q = 0; q < 4; ++q) {
-			const uint4 v = src[q];
-			w[4 * q] = msg_word(v.x);
-			w[4 * q + 1] = msg_word(v.y);
-			w[4 * q + 2] = msg_word(v.z);
-			w[4 * q + 3] = msg_word(v.w);
-		}
-		sha_compress(h, w);
-		uint4 *m = reinterpret_cast<uint4 *>(midstate(a, s, j + 1));
-		m[0] = make_uint4(h[0], h[1], h[2], h[3]);
-		m[1] = make_uint4(h[4], h[5], h[6], h[7]);
-	}
-	asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(256) finalize_kernel(const kllm_table_args a)
@@ -336,8 +388,7 @@ extern "C" uint64_t kllm_table_midstate_stride(int max_blocks, int block_size)
 extern "C" int kllm_table_build_launch(const struct kllm_table_args *a, void *stream)
 {
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
-	const int chain_threads = kChainThreads;
-	chain_kernel<<<(a->num_seqs + chain_threads - 1) / chain_threads, chain_threads, 0, st>>>(*a);
+	chain_kernel<<<(a->num_seqs + kChainLanes - 1) / kChainLanes, 2 * kChainLanes, 0, st>>>(*a);
 	cudaError_t e = cudaGetLastError();
 	if (e != cudaSuccess)
 		return (int)e;
