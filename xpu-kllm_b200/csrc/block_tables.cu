@@ -121,26 +121,41 @@ __device__ __forceinline__ uint32_t *midstate(const kllm_table_args &a, int s, i
 	return a.midstates + ((size_t)s * a.ms_stride + j) * 8;
 }
 
+// a + b + c, kept as written: the sums below are grouped so that each
+// round's critical path is one rotate, one xor and one three-way add.
+__device__ __forceinline__ uint32_t add3(uint32_t a, uint32_t b, uint32_t c)
+{
+	uint32_t r;
+	asm("add.u32 %0, %1, %2;\n\tadd.u32 %0, %0, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+	return r;
+}
+
 // FIPS 180-4 6.2.2 step 4 alone: the 64 rounds over a precomputed schedule,
-// wk[t * stride] = W[t] + K[t].
+// wk[t * stride] = W[t] + K[t]. Per round, x = h + W + K and y = d + x do
+// not depend on the previous round (h and d are e and a of three rounds
+// back), so e' = y + S1(e) + Ch and T1 = x + S1(e) + Ch are one add each
+// after S1, and a' = T1 + S0(a) + Maj one more.
 __device__ __forceinline__ void sha_rounds(uint32_t (&h)[8], const uint32_t *wk, int stride)
 {
 	uint32_t a = h[0], b = h[1], c = h[2], d = h[3];
 	uint32_t e = h[4], f = h[5], g = h[6], hh = h[7];
 #pragma unroll
 	for (int t = 0; t < 64; ++t) {
-		const uint32_t t1 = hh + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) +
-				    ((e & f) ^ (~e & g)) + wk[t * stride];
-		const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) +
-				    ((a & b) ^ (a & c) ^ (b & c));
+		const uint32_t x = hh + wk[t * stride];
+		const uint32_t y = d + x;
+		const uint32_t s1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+		const uint32_t ch = (e & f) ^ (~e & g);
+		const uint32_t s0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+		const uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
+		const uint32_t t1 = add3(s1, ch, x);
 		hh = g;
 		g = f;
 		f = e;
-		e = d + t1;
+		e = add3(s1, ch, y);
 		d = c;
 		c = b;
 		b = a;
-		a = t1 + t2;
+		a = add3(t1, s0, mj);
 	}
 	h[0] += a; h[1] += b; h[2] += c; h[3] += d;
 	h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
