@@ -332,10 +332,12 @@ __device__ void sort_keys_desc(uint32_t *key, int n)
 
 // Candidates for the k largest of a row, when the tile maxima bound them:
 // the k-th largest tile maximum tau is an element, so at least k elements
-// are >= tau and every one of the k largest is. One pass over the row
-// (16-byte loads, four in flight per thread) collects the elements >= tau;
-// returns their number, or -1 when it exceeds the buffer or k exceeds the
-// tiles (the caller then runs the full radix select).
+// are >= tau and every one of the k largest is. Only tiles whose maximum
+// reaches tau can hold such elements (about k of the row's tiles), so one
+// pass over those tiles (16-byte loads, eight in flight per thread)
+// collects the elements >= tau; returns their number, or -1 when it
+// exceeds the buffer or k exceeds the tiles (the caller then runs the full
+// radix select).
 __device__ int tile_bound_candidates(const float *lg, int V, const float *pm, int NT, int k,
 				     SampleSmem &sm)
 {
@@ -346,12 +348,21 @@ __device__ int tile_bound_candidates(const float *lg, int V, const float *pm, in
 		P <<= 1;
 	for (int t = threadIdx.x; t < P; t += kSampThreads)
 		sm.tkeys[t] = t < NT ? order_key(pm[t]) : 0u;
-	if (threadIdx.x == 0)
+	if (threadIdx.x == 0) {
 		sm.count = 0;
+		sm.remain = 0;                  // tiles listed below
+	}
 	__syncthreads();
 	sort_keys_desc(sm.tkeys, P);
 	const uint32_t tau = sm.tkeys[k - 1];
 	__syncthreads();
+	// the tiles to scan, listed over the sorted keys (no longer needed)
+	uint32_t *tiles = sm.tkeys;
+	for (int t = threadIdx.x; t < NT; t += kSampThreads)
+		if (order_key(pm[t]) >= tau)
+			tiles[atomicAdd(&sm.remain, 1)] = (uint32_t)t;
+	__syncthreads();
+	const int nt = sm.remain;
 	auto take = [&](float v, int i) {
 		if (order_key(v) >= tau) {
 			const int pos = atomicAdd(&sm.count, 1);
@@ -362,30 +373,36 @@ __device__ int tile_bound_candidates(const float *lg, int V, const float *pm, in
 		}
 	};
 	if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(lg) & 15u) == 0) {
+		// 64 threads per tile (one float4 each), four tiles side by side
+		constexpr int kVec = kVN / 4, kSide = kSampThreads / kVec, kFly = 8;
 		const float4 *l4 = reinterpret_cast<const float4 *>(lg);
 		const int n4 = V >> 2;
-		for (int base = 0; base < n4; base += 4 * kSampThreads) {
-			float4 x[4];
+		const int sub = threadIdx.x % kVec, side = threadIdx.x / kVec;
+		for (int base = 0; base < nt; base += kSide * kFly) {
+			float4 x[kFly];
+			int j4[kFly];
 #pragma unroll
-			for (int u = 0; u < 4; ++u) {
-				const int j = base + u * kSampThreads + threadIdx.x;
-				x[u] = j < n4 ? l4[j] : make_float4(-CUDART_INF_F, -CUDART_INF_F,
-								    -CUDART_INF_F, -CUDART_INF_F);
+			for (int u = 0; u < kFly; ++u) {
+				const int idx = base + u * kSide + side;
+				j4[u] = idx < nt ? (int)tiles[idx] * kVec + sub : n4;
+				x[u] = j4[u] < n4 ? l4[j4[u]] : make_float4(0.f, 0.f, 0.f, 0.f);
 			}
 #pragma unroll
-			for (int u = 0; u < 4; ++u) {
-				const int j = base + u * kSampThreads + threadIdx.x;
-				if (j < n4) {
-					take(x[u].x, 4 * j);
-					take(x[u].y, 4 * j + 1);
-					take(x[u].z, 4 * j + 2);
-					take(x[u].w, 4 * j + 3);
+			for (int u = 0; u < kFly; ++u) {
+				if (j4[u] < n4) {
+					take(x[u].x, 4 * j4[u]);
+					take(x[u].y, 4 * j4[u] + 1);
+					take(x[u].z, 4 * j4[u] + 2);
+					take(x[u].w, 4 * j4[u] + 3);
 				}
 			}
 		}
 	} else {
-		for (int i = threadIdx.x; i < V; i += kSampThreads)
-			take(lg[i], i);
+		for (int idx = 0; idx < nt; ++idx) {
+			const int i = (int)tiles[idx] * kVN + threadIdx.x;
+			if (i < V)
+				take(lg[i], i);
+		}
 	}
 	__syncthreads();
 	const int n = sm.count;
@@ -539,26 +556,46 @@ __device__ void sort_candidates(SampleSmem &sm, int n)
 }
 
 // The reference's temperature draw over the first k sorted candidates
-// (decode_loop.c:71-113 on the top-k list), sequential as it runs it.
+// (decode_loop.c:71-113 on the top-k list). The max, each p = exp((v - max)
+// / T) and each p / sum do not depend on the order and run on every thread;
+// the two running sums stay sequential, in the reference's order, on one.
 __device__ int draw_sorted(SampleSmem &sm, int k, float T, float r)
 {
+	if (T > 0.f) {
+		float mx = -CUDART_INF_F;
+		for (int j = threadIdx.x; j < k; j += kSampThreads)
+			mx = fmaxf(mx, sm.cand_v[j]);
+#pragma unroll
+		for (int o = 16; o; o >>= 1)
+			mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+		if ((threadIdx.x & 31) == 0)
+			sm.fsh[threadIdx.x >> 5] = mx;
+		__syncthreads();
+		mx = sm.fsh[0];
+		for (int i = 1; i < kSampThreads / 32; ++i)
+			mx = fmaxf(mx, sm.fsh[i]);
+		for (int j = threadIdx.x; j < k; j += kSampThreads)
+			sm.cand_v[j] = expf((sm.cand_v[j] - mx) / T);
+		__syncthreads();
+		if (threadIdx.x == 0) {
+			float sum = 0.f;
+			for (int j = 0; j < k; ++j)
+				sum += sm.cand_v[j];
+			sm.fsh[0] = sum;
+		}
+		__syncthreads();
+		const float sum = sm.fsh[0];
+		for (int j = threadIdx.x; j < k; j += kSampThreads)
+			sm.cand_v[j] = sm.cand_v[j] / sum;
+		__syncthreads();
+	}
 	if (threadIdx.x == 0) {
 		int res = 0;
 		if (T > 0.f) {
-			float mx = -CUDART_INF_F;
-			for (int j = 0; j < k; ++j)
-				if (sm.cand_v[j] > mx)
-					mx = sm.cand_v[j];
-			float sum = 0.f;
-			for (int j = 0; j < k; ++j) {
-				const float p = expf((sm.cand_v[j] - mx) / T);
-				sm.cand_v[j] = p;
-				sum += p;
-			}
 			float cum = 0.f;
 			res = k - 1;
 			for (int j = 0; j < k; ++j) {
-				cum += sm.cand_v[j] / sum;
+				cum += sm.cand_v[j];
 				if (r <= cum) {
 					res = j;
 					break;
