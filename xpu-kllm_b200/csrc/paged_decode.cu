@@ -920,8 +920,8 @@ decode_kernel(const kllm_decode_args a)
 // Wide merge of the queued long segments: one CTA of 8 warps per
 // (segment, query head). Pass 1: the segment's maximum over all its pieces
 // (independent loads by all threads, block reduction). Pass 2: warp w sums
-// pieces w, w+8, ... (o and l, each piece relative to its own maximum m,
-// weighted by exp2(m - maximum)) four pieces in flight, so
+// pieces w, w+8, ... in that order (o and l, each piece relative to its own
+// maximum m, weighted by exp2(m - maximum)) eight pieces in flight, so
 // the loads do not wait on one another; the warps' sums are added in shared
 // memory. The last CTA to finish clears the list header for the next launch.
 template <int D>
@@ -939,6 +939,7 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 	const long long T = lh->T, W = lh->W;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	constexpr int NV = D / 32;
+	constexpr int kFly = 8;   // pieces in flight per warp
 	const long long pairs = (long long)count * a.group;
 
 	for (long long pr = blockIdx.x; pr < pairs; pr += gridDim.x) {
@@ -974,10 +975,10 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 #pragma unroll
 		for (int i = 0; i < NV; ++i)
 			acc[i] = 0.f;
-		for (long long r0 = warp; r0 < np; r0 += 32) {
-			float lr[4], mr[4], ov[4][NV];
+		for (long long r0 = warp; r0 < np; r0 += 8 * kFly) {
+			float lr[kFly], mr[kFly], ov[kFly][NV];
 #pragma unroll
-			for (int u = 0; u < 4; ++u) {
+			for (int u = 0; u < kFly; ++u) {
 				const long long r = r0 + 8 * u;
 				lr[u] = 0.f;
 				mr[u] = 0.f;
@@ -988,14 +989,24 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 					const float *sl = slot_of(r);
 					lr[u] = __ldcg(sl + kSlotL + hh);
 					mr[u] = __ldcg(sl + kSlotM + hh);
+					// 16 (D = 128) or 8 (D = 64) bytes per lane, aligned:
+					// slots are 4,160-byte strided from an aligned base
 					const float *src = sl + kSlotO + hh * D + lane * NV;
-#pragma unroll
-					for (int i = 0; i < NV; ++i)
-						ov[u][i] = __ldcg(src + i);
+					if constexpr (NV == 4) {
+						const float4 v = __ldcg(reinterpret_cast<const float4 *>(src));
+						ov[u][0] = v.x;
+						ov[u][1] = v.y;
+						ov[u][2] = v.z;
+						ov[u][3] = v.w;
+					} else {
+						const float2 v = __ldcg(reinterpret_cast<const float2 *>(src));
+						ov[u][0] = v.x;
+						ov[u][1] = v.y;
+					}
 				}
 			}
 #pragma unroll
-			for (int u = 0; u < 4; ++u) {
+			for (int u = 0; u < kFly; ++u) {
 				// a piece's o is unnormalised (relative to its own max m): it
 				// weighs exp2(m - Mt); its l weighs the same into L
 				const float e = lr[u] > 0.f ? exp2f(mr[u] - Mt) : 0.f;
