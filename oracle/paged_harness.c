@@ -1,7 +1,7 @@
 /* SPDX-License-Identifier: Apache-2.0 */
 /*
  * paged_harness.c - multi-threaded CPU paged decode, timed as the CPU
- * baseline. TEST / BASELINE INFRASTRUCTURE ONLY.
+ * baseline. TEST AND CPU-BASELINE INFRASTRUCTURE ONLY.
  *
  * Built twice by oracle/Makefile:
  *   - liboracle.so: attention = orc_attention (the C restatement, "port");
