@@ -113,11 +113,25 @@ def test_no_device_context_fails_loudly():
         assert lib.kllm_gpu_paged_attention(ctx, ctypes.byref(kb.AttnParams())) == kb.ENODEV
         assert lib.kllm_gpu_malloc(ctx, 1024) is None
         assert lib.kllm_gpu_memcpy_h2d(ctx, None, None, 16) == kb.ENODEV
+        # the table builder and lm_head refuse too, before any launch
+        tp = kb.TableBuildParams()
+        tp.struct_size = ctypes.sizeof(tp)
+        assert lib.kllm_gpu_build_block_tables(ctx, ctypes.byref(tp)) == kb.ENODEV
+        lp = kb.LmHeadParams()
+        lp.struct_size = ctypes.sizeof(lp)
+        assert lib.kllm_gpu_lm_head_sample(ctx, ctypes.byref(lp)) == kb.ENODEV
         st = kb.Stats()
         assert lib.kllm_gpu_get_stats(ctx, ctypes.byref(st)) == 0
-        assert st.errors >= 2 and st.last_error == kb.ENODEV
+        assert st.errors >= 4 and st.last_error == kb.ENODEV
     finally:
         lib.kllm_gpu_destroy(ctx)
+    # workspace sizes are host arithmetic: midstates of 32 B per 16 tokens
+    # (+1) per sequence; 12 B per (row, 256-row vocabulary tile) + 32
+    assert lib.kllm_gpu_table_workspace_size(4, 8, 16) == 4 * (8 * 16 // 16 + 1) * 32
+    assert lib.kllm_gpu_table_workspace_size(3, 5, 24) == 3 * (5 * 24 // 16 + 1) * 32
+    assert lib.kllm_gpu_table_workspace_size(-1, 8, 16) == 0
+    assert lib.kllm_gpu_lm_head_workspace_size(256, 128256) == 256 * 501 * 12 + 32
+    assert lib.kllm_gpu_lm_head_workspace_size(0, 128256) == 0
     # the stateless v1 launcher validates before touching a device
     assert lib.kllm_gpu_paged_attention_cuda(None, None, None, None, 1, 32, 8, 96, 4,
                                              ctypes.c_float(0.1), None) == kb.ENOSYS
