@@ -23,9 +23,12 @@
 // whose running sum of exp((l - max) / T) reaches r x total (tiles in order
 // from the partials, then the chosen tile's columns); top-k = the k largest
 // logits ordered by (value desc, index asc) as the reference's insertion
-// selection orders them, found by a radix select over the row, then the
-// reference's temperature draw over that list, run sequentially as the
-// reference runs it; top-p = temperature (the reference's nucleus is a TODO).
+// selection orders them: the k-th largest tile maximum bounds them from
+// below, so a pass over the tiles whose maximum reaches it collects the
+// candidates and a bitonic sort orders them (a radix select over the row
+// covers k above the tile count or a candidate overflow), then the
+// reference's temperature draw over that list, its running sums in the
+// reference's order; top-p = temperature (the reference's nucleus is a TODO).
 
 #include "kllm_device.cuh"
 #include "kllm_internal.h"
