@@ -16,7 +16,9 @@
 //   S_t = Q_t . K_j^T        tcgen05.mma kind::f16, Q and K in shared memory
 //   P_t = exp2(S_t*c - m)    one softmax thread per row (TMEM lane), written
 //                            back over S_t as bf16 hi + lo
-//   O_t += P_t . V_j         tcgen05.mma with A = P_t read from TMEM
+//   O_t += P_t . V_j         tcgen05.mma with A = P_t read from TMEM, in two
+//                            halves: keys 0-63 start as soon as the softmax
+//                            has written them, while it finishes 64-127
 // Warp roles (13 warps):
 //   0-3 / 4-7  softmax of tile A / B (warp w reads TMEM lanes 32 (w % 4) ..)
 //   8-11       producer: Q tiles, then per block either TMA tensor copies of
