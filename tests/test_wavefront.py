@@ -67,6 +67,13 @@ def test_struct_layouts(tmp_path):
 def test_bad_arguments_refused(tmp_path):
     lib = kb.load()
     assert lib.kllm_wavefront_create(str(tmp_path / "missing").encode()) is None
+    store = tmp_path / "store"
+    store.write_bytes(b"\0" * 4096)
+    # out of range before any device is touched: block size 0 or above 1 GiB,
+    # fewer than 2 or more than 64 staging buffers, a negative device
+    for dev, mb, nbuf in ((0, 0, 8), (0, (1 << 30) + 1, 8), (0, 4096, 1), (0, 4096, 65),
+                          (-1, 4096, 8)):
+        assert lib.kllm_wavefront_create2(str(store).encode(), dev, mb, nbuf) is None
     assert lib.kllm_wavefront_submit(None, None) == -1
     assert lib.kllm_wavefront_poll(None, None, 0) == -1
     assert lib.kllm_wavefront_wait(None, None, 1, 0) == -1
