@@ -207,12 +207,17 @@ int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
  * workspace. Needs no context; the caller passes inputs and outputs (the
  * device is the one `stream` belongs to, or the current device when stream
  * is NULL). Split-KV scratch lives in a fixed 16 MiB device array inside the
- * library, present on every GPU that loads it until the process exits. The
- * first call on a device looks up that array's address (a runtime query):
- * make it before starting any stream capture on that device. Every call
- * shares the array, so calls that overlap on the GPU race; serialise them.
- * Limit: num_seqs * num_kv_heads <= 65536, else KLLM_ENOSPC. The workspace
- * fields of *p are ignored. */
+ * library, present on every GPU that loads it until the process exits.
+ * Set-up: the first call on a device loads the library's decode code and
+ * that array onto the device (CUDA loads device code lazily, which may need
+ * device memory) and looks up the array's address (a runtime query). A call
+ * with num_seqs == 0 does only this: make one per device at start-up,
+ * before the KV arena is allocated and before any stream capture on that
+ * device. Every call shares the array, so calls that overlap on the GPU
+ * race; serialise them. Limit: num_seqs * num_kv_heads <= 65536, else
+ * KLLM_ENOSPC. split < 0 runs one warp per (seq, kv head) and uses no
+ * scratch. The caller's current device is unchanged on return. The
+ * workspace fields of *p are ignored. */
 int kllm_gpu_paged_attention_v2_noalloc(
     const struct kllm_gpu_attention_params_v2 *p);
 

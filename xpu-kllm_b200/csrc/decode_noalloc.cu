@@ -19,10 +19,22 @@
 // slots that fit. Every call reuses the same array, so
 // calls whose kernels overlap on the GPU (different streams, or different
 // host threads) race on it and must be serialised by the caller.
+//
+// Set-up: CUDA loads a library's device code lazily, so the array (and the
+// decode kernels) reach a GPU only when first used there. The first call on
+// a device therefore loads them and looks up the array's address; it may
+// need device memory and issues runtime queries. A call with num_seqs == 0
+// does only this set-up: make one per device at start-up, before the KV
+// arena claims the GPU's memory and before any stream capture.
+//
+// The caller's current device (its current CUDA context) is the same after
+// a call as before it, whichever device the stream belongs to.
 
 #include "kllm_device.cuh"
 #include "kllm_gpu.h"
 #include "kllm_internal.h"
+
+#include <cuda.h>
 
 #include <cstring>
 #include <mutex>
@@ -45,15 +57,59 @@ static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
 std::mutex g_setup_mu;
 unsigned char *g_scratch_ptr[kMaxDevices];  // device address per ordinal
 
-// Looks up the scratch address for `dev` (which must be current). Done once
-// per device; the first call on a device therefore issues a runtime query
-// and should happen before any stream capture is started on that device.
-cudaError_t scratch_for(int dev, unsigned char **out)
+// The calling thread's current context, saved on entry and put back on
+// every return, so a call on another GPU's stream leaves the caller's
+// current device as it was (also when the caller had none yet).
+using ctx_get_fn = CUresult (*)(CUcontext *);
+using ctx_set_fn = CUresult (*)(CUcontext);
+ctx_get_fn g_ctx_get;
+ctx_set_fn g_ctx_set;
+std::once_flag g_ctx_once;
+
+void resolve_ctx_calls()
+{
+	void *fg = nullptr, *fs = nullptr;
+	cudaDriverEntryPointQueryResult qg, qs;
+	if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fg, cudaEnableDefault, &qg) ==
+		cudaSuccess && qg == cudaDriverEntryPointSuccess &&
+	    cudaGetDriverEntryPoint("cuCtxSetCurrent", &fs, cudaEnableDefault, &qs) ==
+		cudaSuccess && qs == cudaDriverEntryPointSuccess && fg && fs) {
+		g_ctx_get = reinterpret_cast<ctx_get_fn>(fg);
+		g_ctx_set = reinterpret_cast<ctx_set_fn>(fs);
+	}
+	(void)cudaGetLastError();
+}
+
+struct CurrentContextGuard {
+	CUcontext saved = nullptr;
+	bool held = false;
+	CurrentContextGuard()
+	{
+		std::call_once(g_ctx_once, resolve_ctx_calls);
+		held = g_ctx_get && g_ctx_get(&saved) == CUDA_SUCCESS;
+	}
+	~CurrentContextGuard()
+	{
+		if (held)
+			(void)g_ctx_set(saved);
+	}
+};
+
+// Per-device set-up, done once per device with that device current: loads
+// the decode kernels (CUDA loads modules lazily, and with them this
+// module's scratch array) and looks up the scratch's device address. Both
+// may need device memory and are runtime calls, so the first call on a
+// device (a call with num_seqs == 0 does only this) belongs before the KV
+// arena claims the GPU's memory and before any stream capture.
+cudaError_t setup_for(int dev, unsigned char **out)
 {
 	std::lock_guard<std::mutex> lk(g_setup_mu);
 	if (!g_scratch_ptr[dev]) {
+		cudaError_t e = static_cast<cudaError_t>(kllm_decode_preload());
+		if (e != cudaSuccess)
+			return e;
 		void *p = nullptr;
-		cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+		e = cudaGetSymbolAddress(&p, g_decode_scratch);
 		if (e != cudaSuccess)
 			return e;
 		g_scratch_ptr[dev] = static_cast<unsigned char *>(p);
@@ -77,50 +133,68 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	    p->block_size > 128 || p->block_size % 16 ||
 	    (p->kv_dtype != KLLM_KV_BF16 && p->kv_dtype != KLLM_KV_MX_FP8_E4M3))
 		return KLLM_ENOSYS;
+	// the kernels index a sequence's tokens with 32-bit integers
+	if ((uint64_t)p->max_blocks_per_seq * (uint64_t)p->block_size > (1ull << 30))
+		return KLLM_EINVAL;
 	// the counters hold one word per (seq, kv head) of the call
 	if ((long long)p->num_seqs * p->num_kv_heads > kMaxSegments)
 		return KLLM_ENOSPC;
-	if (p->num_seqs == 0)
-		return KLLM_OK;
 	const int partial = p->partial_m || p->partial_l || p->partial_o;
-	if (partial && !(p->partial_m && p->partial_l && p->partial_o))
-		return KLLM_EINVAL;
-	if (!p->query || !p->block_tables || !p->seq_lens || (!p->output && !partial))
-		return KLLM_EINVAL;
-	if ((p->layer_stride & 15u) || p->layer < 0 ||
-	    (((uintptr_t)p->query | (uintptr_t)p->output | (uintptr_t)p->partial_o) & 15u))
-		return KLLM_EINVAL;
+	if (p->num_seqs > 0) {
+		if (partial && !(p->partial_m && p->partial_l && p->partial_o))
+			return KLLM_EINVAL;
+		if (!p->query || !p->block_tables || !p->seq_lens ||
+		    (!p->output && !partial))
+			return KLLM_EINVAL;
+		if ((p->layer_stride & 15u) || p->layer < 0 ||
+		    (((uintptr_t)p->query | (uintptr_t)p->output |
+		      (uintptr_t)p->partial_o) & 15u))
+			return KLLM_EINVAL;
+	}
 
 	cudaStream_t st = static_cast<cudaStream_t>(p->stream);
+	CurrentContextGuard guard;
 	int dev = 0;
 	cudaError_t e = st ? cudaStreamGetDevice(st, &dev) : cudaGetDevice(&dev);
 	if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
 		(void)cudaGetLastError();
 		return KLLM_ENODEV;
 	}
+	int cur = -1;
+	if (cudaGetDevice(&cur) != cudaSuccess ||
+	    (cur != dev && cudaSetDevice(dev) != cudaSuccess)) {
+		(void)cudaGetLastError();
+		return KLLM_ENODEV;
+	}
 	int major = 0, sms = 0;
 	cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
 	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-	if (major != 10 || cudaSetDevice(dev) != cudaSuccess) {
+	if (major != 10) {
 		(void)cudaGetLastError();
 		return KLLM_ENODEV;
 	}
 	unsigned char *scratch = nullptr;
-	if (scratch_for(dev, &scratch) != cudaSuccess) {
+	if (setup_for(dev, &scratch) != cudaSuccess) {
 		(void)cudaGetLastError();
 		return KLLM_EIO;
 	}
+	if (p->num_seqs == 0)
+		return KLLM_OK;
 	unsigned *cnt = reinterpret_cast<unsigned *>(scratch);
 	float *part = reinterpret_cast<float *>(scratch + kCounterBytes);
-
-	// The counters must start at zero; the array keeps whatever the last call
-	// left, so clear the words this call uses (no allocation involved).
-	const size_t segs = (size_t)p->num_seqs * p->num_kv_heads;
 	void *list = scratch + kListOffset;
-	if (cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess ||
-	    cudaMemsetAsync(list, 0, 32, st) != cudaSuccess) {
-		(void)cudaGetLastError();
-		return KLLM_EIO;
+
+	// split < 0: one warp per (seq, kv head), no scratch used (as in v2).
+	const int split = p->split >= 0;
+	if (split) {
+		// The counters must start at zero; the array keeps whatever the last
+		// call left, so clear the words this call uses (no allocation involved).
+		const size_t segs = (size_t)p->num_seqs * p->num_kv_heads;
+		if (cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess ||
+		    cudaMemsetAsync(list, 0, 32, st) != cudaSuccess) {
+			(void)cudaGetLastError();
+			return KLLM_EIO;
+		}
 	}
 
 	struct kllm_decode_args a;
@@ -143,10 +217,10 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	a.pl = p->partial_l;
 	a.po = p->partial_o;
 	a.err = p->err_word;
-	a.split = 1;
-	a.ws_part = part;
-	a.ws_cnt = cnt;
-	a.ws_list = list;
+	a.split = split;
+	a.ws_part = split ? part : nullptr;
+	a.ws_cnt = split ? cnt : nullptr;
+	a.ws_list = split ? list : nullptr;
 
 	const size_t row = (size_t)p->num_heads * p->head_dim;
 	for (int s0 = 0; s0 < p->num_seqs; s0 += KLLM_MAX_SEQS_LAUNCH) {
@@ -160,7 +234,8 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 		c.table = static_cast<const uint8_t *>(p->block_tables) +
 			  (size_t)s0 * p->max_blocks_per_seq * sizeof(struct kllm_block_table_entry);
 		c.seq_lens = p->seq_lens + s0;
-		c.ws_cnt = cnt + (size_t)s0 * p->num_kv_heads;
+		if (split)
+			c.ws_cnt = cnt + (size_t)s0 * p->num_kv_heads;
 		if (partial) {
 			c.pm = p->partial_m + (size_t)s0 * p->num_heads;
 			c.pl = p->partial_l + (size_t)s0 * p->num_heads;
@@ -170,7 +245,7 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 		if (ctas <= 0)
 			return KLLM_EIO;
 		int grid = sms * ctas;
-		if (grid * KLLM_DEC_WARPS > kMaxWarps)
+		if (split && grid * KLLM_DEC_WARPS > kMaxWarps)
 			grid = kMaxWarps / KLLM_DEC_WARPS;
 		c.total_warps = grid * KLLM_DEC_WARPS;
 		if (kllm_decode_launch(&c, grid, st) != 0 ||
