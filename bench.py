@@ -46,6 +46,12 @@ METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200
 # about B x this ratio.
 DECODE_TRAFFIC_RATIO = 1.0162
 
+# What the decode computes in, per KV format: MX-FP8 pages are dequantised in
+# registers to f16 (exact E4M3 x E4M3 products, scaled by 2^-2) and contracted
+# by f16 tensor-core MMAs with fp32 accumulation; BF16 pages by bf16 MMAs.
+DECODE_DTYPE = {wl.KV_MX_FP8: "f16 MMA, fp32 accum (MX-FP8 E4M3 KV dequantised in registers)",
+                wl.KV_BF16: "bf16 MMA, fp32 accum (BF16 KV)"}
+
 
 def peaks() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -174,6 +180,7 @@ class DecodeRig:
         torch.cuda.synchronize()
 
     split_kv = False
+    entry = "context"   # "noalloc": kllm_gpu_paged_attention_v2_noalloc (no context workspace)
 
     def enable_split_kv(self, rank: int, world: int, dist, merge: str = "p2p") -> None:
         """Cross-GPU split-KV: partial triples per rank, exchanged and merged
@@ -225,7 +232,16 @@ class DecodeRig:
         if self.split_kv:
             kw.update(output=None, partial_m=self.pm.data_ptr(), partial_l=self.pl.data_ptr(),
                       partial_o=self.po.data_ptr())
-        rc = self.be.decode_v2(**kw)
+        if self.entry == "noalloc":
+            import ctypes
+            import kllm_b200 as kb
+            p = kb.AttnParamsV2()
+            p.struct_size = ctypes.sizeof(p)
+            for k, v in kw.items():
+                setattr(p, k, v)
+            rc = self.be.lib.kllm_gpu_paged_attention_v2_noalloc(ctypes.byref(p))
+        else:
+            rc = self.be.decode_v2(**kw)
         if rc != 0:
             raise RuntimeError(f"decode launch failed: {rc}")
         if self.split_kv and self.merge == "p2p":
@@ -307,6 +323,12 @@ def run_kllm(args) -> None:
         lo, hi = mg.page_ranges(pages, world)[rank]
         local_len = int(np.clip(lens_all[0] - lo * cfg.block, 0, (hi - lo) * cfg.block))
         mine, lens_rank = [0], np.array([local_len], np.int32)
+    elif args.shard_of:
+        # one rank's share of an N-way request split, timed alone on this GPU
+        # (what each GPU of an N-GPU run does; no other rank exists)
+        r_e, n_e = (int(x) for x in args.shard_of.split("/"))
+        mine = mg.lpt_shard(lens_all, n_e)[r_e]
+        lens_rank = lens_all
     else:
         mine = mg.lpt_shard(lens_all, world)[rank]
         lens_rank = lens_all
@@ -316,6 +338,10 @@ def run_kllm(args) -> None:
     sp = stream.cuda_stream
     if split_kv:
         rig.enable_split_kv(rank, world, dist, args.merge)
+    if args.decode_entry == "noalloc":
+        if split_kv:
+            raise SystemExit("--decode-entry noalloc times the single-GPU decode only")
+        rig.entry = "noalloc"
 
     def barrier():
         if world > 1:
@@ -445,8 +471,8 @@ def run_kllm(args) -> None:
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (seeded; KV quantized on device by the "
-                                     "append kernel)",
+            "dtype": DECODE_DTYPE[cfg.kv_dtype],
+            "data": "synthetic (seeded; KV quantized on device by the append kernel)",
             "config": {"workload": cfg.name, "batch": cfg.batch, "layers": cfg.layers,
                        "hq": cfg.hq, "hkv": cfg.hkv, "head_dim": cfg.d, "block": cfg.block,
                        "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)",
@@ -475,6 +501,11 @@ def run_kllm(args) -> None:
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
+        if args.decode_entry == "noalloc":
+            line["config"]["decode_entry"] = "kllm_gpu_paged_attention_v2_noalloc"
+        if args.shard_of:
+            line["config"]["shard_of"] = (f"requests of rank {args.shard_of} (LPT) only, "
+                                          f"on one GPU: value is that rank's share")
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if per_req is not None:
@@ -484,6 +515,9 @@ def run_kllm(args) -> None:
                 "note": "the same step with one decode launch per request per layer, the "
                         "pattern of userspace/reactor/batch_scheduler.c:258-263"}
         print(json.dumps(line), flush=True)
+        if cpu is not None and not cpu["gpu_matches_reference_on_sample"]:
+            raise SystemExit("bench: the GPU decode of the sampled requests differs from the "
+                             "reference CPU attention beyond 1e-3 + 2e-2|ref|")
     torch.cuda.synchronize()
     torch.cuda.set_stream(torch.cuda.default_stream())
     be.close()
@@ -814,7 +848,8 @@ def run_prefill(args) -> None:
             "value": round(rig.n_tok * args.steps / (t_ms * 1e-3), 1), "unit": "tokens/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 MMA (tcgen05), fp32 accum; MX-FP8 cached K/V dequantised to bf16",
             "data": "synthetic (seeded torch.randn BF16 Q/K/V ~ N(0,1))",
             "config": {"workload": cfg.name, "prompts": cfg.batch, "prompt_len": cfg.ctx_lo,
                        "shared_prefix_hits": int((rig.ctx > 0).sum()),
@@ -873,7 +908,8 @@ def run_reference_prefill(args) -> None:
         "unit": "tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * n_tok / value, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 products, fp32 accum (CPU)",
+        "data": "synthetic",
         "config": {"workload": cfg.name, "prompts": cfg.batch, "prompt_len": cfg.ctx_lo},
         "cpu_baseline": dict(samples[-1], value=round(value, 2)),
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -1329,7 +1365,7 @@ def run_lm_head(args) -> None:
             "metric": LM_HEAD_METRIC, "value": round(R * args.steps / (t_ms * 1e-3), 1),
             "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None, "dtype": "bf16 MMA (tcgen05), fp32 accum",
             "data": "synthetic (seeded torch.randn hidden states and weights)",
             "config": {"workload": c.name, "rows": R, "hidden": H, "vocab": V,
                        "sampling": c.sampling,
@@ -1544,7 +1580,9 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 products, fp32 accum (CPU; MX-FP8 KV dequantised to bf16 exactly)",
+        "data": "synthetic",
         "config": {"workload": cfg.name, "batch": cfg.batch, "layers": cfg.layers,
                    "hq": cfg.hq, "hkv": cfg.hkv, "head_dim": cfg.d, "block": cfg.block,
                    "kv_format": "mx-fp8-e4m3 (e4m3 scale per 8)"},
@@ -1583,6 +1621,12 @@ def main():
     ap.add_argument("--per-request-compare", action="store_true",
                     help="also time the decode step issued one request per launch (the "
                          "reference scheduler's loop), reported beside the batched step")
+    ap.add_argument("--shard-of", default=None, metavar="R/N",
+                    help="decode only the requests rank R of an N-way split would own, on "
+                         "one GPU (per-GPU behaviour of an N-GPU run)")
+    ap.add_argument("--decode-entry", default="context", choices=["context", "noalloc"],
+                    help="decode through kllm_gpu_paged_attention_v2 (context workspace) or "
+                         "kllm_gpu_paged_attention_v2_noalloc (fixed in-library scratch)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (smaller captures for profiling)")
     args = ap.parse_args()

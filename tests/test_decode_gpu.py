@@ -76,8 +76,12 @@ def test_gqa_groups(be, kv, hq, hkv):
 
 
 @pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
-def test_head_dim_64(be, kv):
-    cfg = replace(wl.C1, d=64, hq=16, hkv=4, kv_dtype=kv, arena_slots=None)
+@pytest.mark.parametrize("hq,hkv", [(16, 4), (4, 4), (8, 4), (32, 4)])
+def test_head_dim_64(be, kv, hq, hkv):
+    """d = 64 at every merge lane layout (groups 1, 2, 4, 8): short contexts
+    are split one tile per warp, so segments of up to 16 tiles are merged by
+    the decode itself and longer ones by the wide merge."""
+    cfg = replace(wl.C1, d=64, hq=hq, hkv=hkv, kv_dtype=kv, arena_slots=None)
     hc = kvcase.build_case(cfg, seq_lens=[4, 100, 257, 16, 0])
     dc = kvcase.DeviceCase(hc)
     kvcase.assert_close_bf16(run_v2(be, dc), hc.oracle_decode(), what="d=64")

@@ -53,7 +53,9 @@ struct kllm_decode_args {
 /* Segments split over more than KLLM_FUSED_MERGE_MAX warps are not merged by
  * the last warp of the decode but queued for kllm_decode_merge_launch, which
  * merges each (segment, query head) with a whole CTA. */
+#ifndef KLLM_FUSED_MERGE_MAX
 #define KLLM_FUSED_MERGE_MAX   16
+#endif
 #define KLLM_MERGE_LIST_CAP    1024
 #define KLLM_MERGE_LIST_BYTES  (32 + 24 * KLLM_MERGE_LIST_CAP)
 
@@ -65,6 +67,9 @@ int kllm_decode_merge_launch(const struct kllm_decode_args *a, int num_sms,
 size_t kllm_decode_smem_bytes(int head_dim, int kv_dtype, int num_seqs);
 /* Resident CTAs per SM for this shape (0 on error). */
 int kllm_decode_ctas_per_sm(int head_dim, int kv_dtype, int num_seqs);
+/* Loads every decode and wide-merge kernel on the current device now
+ * instead of at first launch; 0 or a cudaError_t. */
+int kllm_decode_preload(void);
 /* Launches the decode on `stream` with `grid` CTAs; 0 or a cudaError_t. */
 int kllm_decode_launch(const struct kllm_decode_args *a, int grid,
 		       void *stream);

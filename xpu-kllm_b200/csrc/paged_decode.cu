@@ -529,47 +529,111 @@ __device__ void write_empty_seq(const kllm_decode_args &a, int s, int lane)
 	}
 }
 
-// Log-sum-exp merge of the pieces of one segment, run by the warp that
-// finished last. Lane -> (head lane/4, dims (lane%4)*D/4 ..).
-template <int D>
-__device__ void merge_segment(const kllm_decode_args &a, const Seg &sg,
-			      long long seg_x0, long long T, long long W,
-			      float unbias, int lane)
+// NL consecutive floats from 8- or 16-byte aligned global memory (L2 only).
+template <int NL>
+__device__ __forceinline__ void ldcg_vec(float (&v)[NL], const float *src)
 {
-	const long long w0 = owner_warp(seg_x0, T, W);
-	const long long w1 = owner_warp(seg_x0 + sg.ts - 1, T, W);
-	const int hh = lane >> 2, part = lane & 3;
-	constexpr int NV = D / 4;  // values per lane
-	float acc[NV];
+	if constexpr (NL % 4 == 0) {
 #pragma unroll
-	for (int i = 0; i < NV; ++i)
-		acc[i] = 0.f;
-	float M = -CUDART_INF_F, L = 0.f;
-	const bool active = hh < a.group;
+		for (int i = 0; i < NL / 4; ++i) {
+			const float4 x = __ldcg(reinterpret_cast<const float4 *>(src) + i);
+			v[4 * i] = x.x;
+			v[4 * i + 1] = x.y;
+			v[4 * i + 2] = x.z;
+			v[4 * i + 3] = x.w;
+		}
+	} else {
+		static_assert(NL == 2, "two or a multiple of four floats");
+		const float2 x = __ldcg(reinterpret_cast<const float2 *>(src));
+		v[0] = x.x;
+		v[1] = x.y;
+	}
+}
 
-	for (long long wr = w0; wr <= w1; ++wr) {
-		const long long b = wr * T / W;
-		const int which = (wr == w0 && b != seg_x0) ? 1 : 0;
-		const float *slot = a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
-		if (!active)
-			continue;
-		const float mr = __ldcg(slot + kSlotM + hh);
-		const float lr = __ldcg(slot + kSlotL + hh);
-		if (!(lr > 0.f))
-			continue;
-		const float mn = fmaxf(M, mr);
-		const float fo = exp2f(M - mn), fr = exp2f(mr - mn);
-		L = L * fo + lr * fr;
-		M = mn;
-		const float4 *src = reinterpret_cast<const float4 *>(
-		    slot + kSlotO + hh * D + part * NV);
+// Log-sum-exp merge of the pieces of one segment, run by the warp that
+// finished last; it sits on that warp's critical path (the last arriver of a
+// segment is usually the warp whose range ends inside it), so every load is
+// issued without waiting on another. GP = the segment's query heads rounded
+// up to a power of two; lane -> (head lane / (32/GP), NL dims from
+// (lane % (32/GP)) * NL), so all 32 lanes work at every group size.
+// Pass 1: each head's maximum over the pieces with mass (the 32/GP lanes of
+// a head take every (32/GP)-th piece, four pieces per load batch). Pass 2:
+// the pieces' o and l summed against that maximum, KB pieces in flight.
+template <int D, int GP>
+__device__ __forceinline__ void merge_segment_gp(const kllm_decode_args &a, const Seg &sg,
+					      long long seg_x0, long long T, long long W,
+					      float unbias, int lane)
+{
+	constexpr int LPH = 32 / GP;            // lanes per head
+	constexpr int NL = D / LPH;             // dims per lane
+	constexpr int KB = NL >= 32 ? 1 : 32 / NL;  // pieces in flight in pass 2
+	const long long w0 = owner_warp(seg_x0, T, W);
+	const int np = (int)(owner_warp(seg_x0 + sg.ts - 1, T, W) - w0 + 1);
+	const int hh = lane / LPH, part = lane % LPH;
+	const bool active = hh < a.group;
+	auto slot_of = [&](int r) -> const float * {
+		const long long wr = w0 + r;
+		const int which = (r == 0 && wr * T / W != seg_x0) ? 1 : 0;
+		return a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
+	};
+
+	// ---- pass 1: the head's maximum (log2 domain) over pieces with mass ----
+	float M = -CUDART_INF_F;
+	for (int r0 = 0; r0 < np; r0 += 4 * LPH) {
+		float mr[4], lr[4];
 #pragma unroll
-		for (int i = 0; i < NV / 4; ++i) {
-			const float4 v = __ldcg(src + i);
-			acc[4 * i] = acc[4 * i] * fo + v.x * fr;
-			acc[4 * i + 1] = acc[4 * i + 1] * fo + v.y * fr;
-			acc[4 * i + 2] = acc[4 * i + 2] * fo + v.z * fr;
-			acc[4 * i + 3] = acc[4 * i + 3] * fo + v.w * fr;
+		for (int u = 0; u < 4; ++u) {
+			const int r = r0 + part + u * LPH;
+			mr[u] = -CUDART_INF_F;
+			lr[u] = 0.f;
+			if (active && r < np) {
+				const float *sl = slot_of(r);
+				mr[u] = __ldcg(sl + kSlotM + hh);
+				lr[u] = __ldcg(sl + kSlotL + hh);
+			}
+		}
+#pragma unroll
+		for (int u = 0; u < 4; ++u)
+			if (lr[u] > 0.f)
+				M = fmaxf(M, mr[u]);
+	}
+#pragma unroll
+	for (int off = 1; off < LPH; off <<= 1)
+		M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+
+	// ---- pass 2: weighted sums of o and l against M -------------------------
+	float acc[NL];
+#pragma unroll
+	for (int i = 0; i < NL; ++i)
+		acc[i] = 0.f;
+	float L = 0.f;
+	for (int r0 = 0; r0 < np; r0 += KB) {
+		float mr[KB], lr[KB], ov[KB][NL];
+#pragma unroll
+		for (int u = 0; u < KB; ++u) {
+			const int r = r0 + u;
+			mr[u] = 0.f;
+			lr[u] = 0.f;
+			if (active && r < np) {
+				const float *sl = slot_of(r);
+				mr[u] = __ldcg(sl + kSlotM + hh);
+				lr[u] = __ldcg(sl + kSlotL + hh);
+				// slots are 4,160-byte strided from a 256-byte aligned base
+				ldcg_vec<NL>(ov[u], sl + kSlotO + hh * D + part * NL);
+			} else {
+#pragma unroll
+				for (int i = 0; i < NL; ++i)
+					ov[u][i] = 0.f;
+			}
+		}
+#pragma unroll
+		for (int u = 0; u < KB; ++u) {
+			// a piece's o is relative to its own maximum m: it weighs exp2(m - M)
+			const float e = lr[u] > 0.f ? exp2f(mr[u] - M) : 0.f;
+			L = fmaf(lr[u], e, L);
+#pragma unroll
+			for (int i = 0; i < NL; ++i)
+				acc[i] = fmaf(ov[u][i], e, acc[i]);
 		}
 	}
 	if (!active)
@@ -577,26 +641,53 @@ __device__ void merge_segment(const kllm_decode_args &a, const Seg &sg,
 	const size_t row = (size_t)sg.s * a.num_heads + (size_t)sg.h * a.group + hh;
 	const float inv = L > 0.f ? unbias / L : 0.f;
 	if (a.pm) {
-		float *po = a.po + row * D + part * NV;
+		float *po = a.po + row * D + part * NL;
+		if constexpr (NL % 4 == 0) {
 #pragma unroll
-		for (int i = 0; i < NV; i += 4)
-			*reinterpret_cast<float4 *>(po + i) = make_float4(
-			    acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv,
-			    acc[i + 3] * inv);
+			for (int i = 0; i < NL; i += 4)
+				*reinterpret_cast<float4 *>(po + i) = make_float4(
+				    acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv,
+				    acc[i + 3] * inv);
+		} else {
+			*reinterpret_cast<float2 *>(po) = make_float2(acc[0] * inv, acc[1] * inv);
+		}
 		if (part == 0) {
 			a.pm[row] = L > 0.f ? M * 0.69314718055994531f : -CUDART_INF_F;
 			a.pl[row] = L;
 		}
 	} else {
-		uint8_t *po = reinterpret_cast<uint8_t *>(a.out) + (row * D + part * NV) * 2;
+		uint8_t *po = reinterpret_cast<uint8_t *>(a.out) + (row * D + part * NL) * 2;
+		if constexpr (NL % 8 == 0) {
 #pragma unroll
-		for (int i = 0; i < NV; i += 8)
-			*reinterpret_cast<uint4 *>(po + i * 2) = make_uint4(
-			    pack_bf16x2(acc[i] * inv, acc[i + 1] * inv),
-			    pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
-			    pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv),
-			    pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
+			for (int i = 0; i < NL; i += 8)
+				*reinterpret_cast<uint4 *>(po + i * 2) = make_uint4(
+				    pack_bf16x2(acc[i] * inv, acc[i + 1] * inv),
+				    pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
+				    pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv),
+				    pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
+		} else if constexpr (NL == 4) {
+			*reinterpret_cast<uint2 *>(po) = make_uint2(
+			    pack_bf16x2(acc[0] * inv, acc[1] * inv),
+			    pack_bf16x2(acc[2] * inv, acc[3] * inv));
+		} else {
+			*reinterpret_cast<uint32_t *>(po) = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+		}
 	}
+}
+
+template <int D>
+__device__ __forceinline__ void merge_segment(const kllm_decode_args &a, const Seg &sg,
+					      long long seg_x0, long long T, long long W,
+					      float unbias, int lane)
+{
+	if (a.group > 4)
+		merge_segment_gp<D, 8>(a, sg, seg_x0, T, W, unbias, lane);
+	else if (a.group > 2)
+		merge_segment_gp<D, 4>(a, sg, seg_x0, T, W, unbias, lane);
+	else if (a.group > 1)
+		merge_segment_gp<D, 2>(a, sg, seg_x0, T, W, unbias, lane);
+	else
+		merge_segment_gp<D, 1>(a, sg, seg_x0, T, W, unbias, lane);
 }
 
 template <int D, int KVT>
@@ -1113,6 +1204,22 @@ extern "C" int kllm_decode_ctas_per_sm(int head_dim, int kv_dtype, int num_seqs)
 		return kv_dtype ? Launcher<64, 1>::occupancy(num_seqs)
 				: Launcher<64, 0>::occupancy(num_seqs);
 	return 0;
+}
+
+extern "C" int kllm_decode_preload(void)
+{
+	// Querying a kernel's attributes makes the runtime load it now (CUDA
+	// loads modules lazily by default), so later launches need no memory
+	// for code.
+	cudaFuncAttributes fa;
+	cudaError_t e = cudaSuccess;
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, decode_kernel<128, 0>);
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, decode_kernel<128, 1>);
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, decode_kernel<64, 0>);
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, decode_kernel<64, 1>);
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, merge_big_kernel<128>);
+	if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, merge_big_kernel<64>);
+	return (int)e;
 }
 
 extern "C" int kllm_decode_merge_launch(const struct kllm_decode_args *a,
