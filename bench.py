@@ -181,6 +181,9 @@ class DecodeRig:
 
     split_kv = False
     entry = "context"   # "noalloc": kllm_gpu_paged_attention_v2_noalloc (no context workspace)
+    # consecutive layers' decodes: each may start while the previous one
+    # finishes (the block table and seq_lens are not written between them)
+    flags = 0x1         # KLLM_DECODE_OVERLAP_PREV
 
     def enable_split_kv(self, rank: int, world: int, dist, merge: str = "p2p") -> None:
         """Cross-GPU split-KV: partial triples per rank, exchanged and merged
@@ -228,7 +231,8 @@ class DecodeRig:
             block_tables=self.table.data_ptr(), seq_lens=self.seq_lens.data_ptr(),
             num_seqs=self.B, num_heads=c.hq, num_kv_heads=c.hkv, head_dim=c.d,
             max_blocks_per_seq=self.plan.max_blocks, block_size=c.block, kv_dtype=c.kv_dtype,
-            layer=layer, layer_stride=self.layer_stride, scale=c.scale, split=1, stream=stream)
+            layer=layer, layer_stride=self.layer_stride, scale=c.scale, split=1, stream=stream,
+            flags=self.flags)
         if self.split_kv:
             kw.update(output=None, partial_m=self.pm.data_ptr(), partial_l=self.pl.data_ptr(),
                       partial_o=self.po.data_ptr())
@@ -342,6 +346,9 @@ def run_kllm(args) -> None:
         if split_kv:
             raise SystemExit("--decode-entry noalloc times the single-GPU decode only")
         rig.entry = "noalloc"
+        rig.flags = 0
+    if args.no_overlap:
+        rig.flags = 0
 
     def barrier():
         if world > 1:
@@ -479,6 +486,9 @@ def run_kllm(args) -> None:
                        "kv_gb_per_step": round(total_bytes / 1e9, 3),
                        "arena_gb_rank0": round(float(allst[0, 5]) / 1e9, 2),
                        "arena_layout": args.arena_layout,
+                       "decode_launch": ("programmatic dependent of the previous layer's "
+                                         "kernels (KLLM_DECODE_OVERLAP_PREV)" if rig.flags
+                                         else "after the previous kernel completed"),
                        "l2": "inputs larger than L2 (KV per step >> 126 MB)",
                        "parallelism": ((f"split-KV x{world} (page ranges) + one peer-memory "
                                         f"exchange-and-merge kernel per rank (NVLink)"
@@ -1621,6 +1631,9 @@ def main():
     ap.add_argument("--per-request-compare", action="store_true",
                     help="also time the decode step issued one request per launch (the "
                          "reference scheduler's loop), reported beside the batched step")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch each layer's decode only after the previous kernel completed "
+                         "(no KLLM_DECODE_OVERLAP_PREV)")
     ap.add_argument("--shard-of", default=None, metavar="R/N",
                     help="decode only the requests rank R of an N-way split would own, on "
                          "one GPU (per-GPU behaviour of an N-GPU run)")

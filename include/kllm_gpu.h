@@ -134,6 +134,9 @@ int kllm_gpu_paged_attention_cuda(
 #define KLLM_ERR_APPEND_NOPAGE  0x4u  /* append target page invalid / position out of table */
 #define KLLM_ERR_TIMEOUT        0x8u  /* a bounded device-side wait expired; the warp stopped */
 #define KLLM_ERR_TOPK_RANGE     0x10u /* lm_head: top_k in (1024, vocab): token -1 for that row */
+#define KLLM_ERR_NONFINITE      0x20u /* decode: an MX-FP8 page holds payload 0x7F / 0xFF and the
+                                        segment could not be recomputed exactly (split < 0, or
+                                        the wide-merge queue was full): its rows are not finite */
 
 /* KV page formats. One page holds `block_size` tokens of one layer.
  *
@@ -144,9 +147,10 @@ int kllm_gpu_paged_attention_cuda(
  *   [block_size][head_dim/8] E4M3 scale bytes (one scale per 8 consecutive
  *   elements along head_dim, userspace/compute/mx_dequant.h:27). Real value =
  *   e4m3(payload) * e4m3(scale), decoded as userspace/compute/mx_dequant.h:30-55
- *   (0x7F/0xFF decode to +-480; the decode kernel converts payloads with the
- *   hardware OCP E4M3 conversion, which reads payload 0x7F/0xFF as NaN; the
- *   append never writes them). V page alike.
+ *   (0x7F/0xFF decode to +-480). The append never writes payload 0x7F/0xFF;
+ *   the decode's tile loop converts with the hardware OCP E4M3 conversion,
+ *   which reads them as NaN, and a segment where that happened is recomputed
+ *   exactly (with split >= 0; see KLLM_ERR_NONFINITE). V page alike.
  *
  * KLLM_KV_MX_BF16_COMPAT: the reference's own MX layout
  *   (userspace/compute/mx_dequant.h:10-16): sections of [block_size][head_dim]
@@ -159,10 +163,20 @@ enum kllm_kv_dtype {
 	KLLM_KV_MX_BF16_COMPAT = 2,
 };
 
+/* kllm_gpu_attention_params_v2.flags */
+/* The decode may begin while the kernel issued just before it on the same
+ * stream is still finishing (programmatic dependent launch): it reads
+ * block_tables and seq_lens before that kernel has completed, and the query,
+ * the pages and every output only after. Set it only when that previous
+ * kernel writes neither block_tables nor seq_lens (for example consecutive
+ * layers of one step, or a KV append followed by the decode); it hides most
+ * of the launch and set-up time of each layer's decode. */
+#define KLLM_DECODE_OVERLAP_PREV 0x1u
+
 /* Decode attention, versioned. Zero-initialise, set struct_size, fill in. */
 struct kllm_gpu_attention_params_v2 {
 	uint32_t struct_size;        /* sizeof(struct kllm_gpu_attention_params_v2) */
-	uint32_t flags;              /* reserved, 0 */
+	uint32_t flags;              /* 0 or KLLM_DECODE_OVERLAP_PREV */
 	void *output;                /* bf16 [num_seqs][num_heads][head_dim]; may be NULL
 	                                when partial_m/l/o are given */
 	const void *query;           /* bf16 [num_seqs][num_heads][head_dim] */

@@ -111,6 +111,8 @@ def test_no_device_context_fails_loudly():
         p.struct_size = ctypes.sizeof(p)
         assert lib.kllm_gpu_paged_attention_v2(ctx, ctypes.byref(p)) == kb.ENODEV
         assert lib.kllm_gpu_paged_attention(ctx, ctypes.byref(kb.AttnParams())) == kb.ENODEV
+        p.flags = 0x2           # not a defined flag: refused before anything else
+        assert lib.kllm_gpu_paged_attention_v2(ctx, ctypes.byref(p)) == kb.EINVAL
         assert lib.kllm_gpu_malloc(ctx, 1024) is None
         assert lib.kllm_gpu_memcpy_h2d(ctx, None, None, 16) == kb.ENODEV
         # the table builder and lm_head refuse too, before any launch

@@ -286,3 +286,88 @@ def test_c4_long_context_wide_merge(be):
     kvcase.assert_close_f32(po.cpu().numpy(), o, what="o")
     # a second call finds the merge queue empty again
     kvcase.assert_close_bf16(run_v2(be, dc), ref, what="C4 again")
+
+
+def test_overlap_flag_layers_and_append(be):
+    """KLLM_DECODE_OVERLAP_PREV: each decode may start while the kernel before
+    it finishes. Three layers decoded back to back into separate outputs, and
+    a decode issued right after a KV append that rewrites the last token of
+    every sequence: the decode must see the appended bytes (it reads pages
+    only after the previous kernel completed)."""
+    import torch
+    cfg = replace(wl.C2, batch=6, layers=3)
+    hc = kvcase.build_case(cfg, seq_lens=[700, 16, 1, 2049, 333, 4096])
+    c = hc.cfg
+    dc = kvcase.DeviceCase(hc)
+    st = torch.cuda.current_stream().cuda_stream
+    outs = [torch.zeros_like(dc.out) for _ in range(c.layers)]
+    for layer in range(c.layers):
+        rc = be.decode_v2(**dc.decode_kwargs(layer=layer, output=outs[layer].data_ptr(),
+                                             flags=kb.DECODE_OVERLAP_PREV, stream=st))
+        assert rc == 0
+    torch.cuda.synchronize()
+    for layer in range(c.layers):
+        got = outs[layer].cpu().numpy().view(np.uint16)
+        kvcase.assert_close_bf16(got, hc.oracle_decode(layer=layer), what=f"layer {layer}")
+
+    # append -> decode (layer 1), the decode launched as a dependent of the append
+    import oracle
+    S = c.batch
+    tok_seq = np.arange(S, dtype=np.int32)
+    tok_pos = (hc.seq_lens - 1).astype(np.int32)
+    k = wl.normal_bf16(5, wl.ST_PK, 0, (S, c.hkv, c.d), mult=3.0)
+    v = wl.normal_bf16(5, wl.ST_PV, 0, (S, c.hkv, c.d), mult=3.0)
+    tk = torch.from_numpy(k.view(np.int16)).cuda()
+    tv = torch.from_numpy(v.view(np.int16)).cuda()
+    ts = torch.from_numpy(tok_seq).cuda()
+    tp = torch.from_numpy(tok_pos).cuda()
+    rc = be.append(k=tk.data_ptr(), v=tv.data_ptr(), token_seq=ts.data_ptr(),
+                   token_pos=tp.data_ptr(), num_tokens=S, num_seqs=S,
+                   block_tables=dc.table.data_ptr(), max_blocks_per_seq=hc.plan.max_blocks,
+                   num_kv_heads=c.hkv, head_dim=c.d, block_size=c.block, kv_dtype=c.kv_dtype,
+                   layer=1, layer_stride=c.layer_stride(), stream=st)
+    assert rc == 0
+    dc.out.fill_(0x7FC0)
+    rc = be.decode_v2(**dc.decode_kwargs(layer=1, flags=kb.DECODE_OVERLAP_PREV, stream=st))
+    assert rc == 0
+    got = dc.out_host()
+    n = oracle.kv_append(k, v, tok_seq, tok_pos, hc.host_table(), hc.plan.max_blocks, c.hkv,
+                         c.d, c.block, c.kv_dtype, hc.layer_off(1))
+    assert n == 0, f"oracle append skipped {n} rows"
+    kvcase.assert_close_bf16(got, hc.oracle_decode(layer=1), what="decode after append")
+    # unknown flag bits are refused
+    assert be.decode_v2(**dc.decode_kwargs(flags=0x2)) == kb.EINVAL
+
+
+@pytest.mark.parametrize("split", [1, -1])
+def test_mx_decode_every_payload_code(be, split):
+    """Every E4M3 payload code through the decode kernel, 0x7F / 0xFF
+    included (the reference decodes them as +-480, the hardware conversion
+    as NaN: such pieces are recomputed exactly). Payload bytes of every K
+    and V page are overwritten with a pattern that cycles through all 256
+    codes; the scale bytes stay the quantizer's. One long context is split
+    over many warps (partials and merges), the others are short."""
+    cfg = replace(wl.C2, batch=4)
+    hc = kvcase.build_case(cfg, seq_lens=[5000, 37, 700, 16])
+    c = hc.cfg
+    sec, pay = c.section_bytes(), c.block * c.d
+    t = np.arange(c.block)[:, None]
+    d = np.arange(c.d)[None, :]
+    for s_, L in enumerate(hc.seq_lens):
+        n_pages = (int(L) + c.block - 1) // c.block
+        for b in range(n_pages):
+            slot = hc.plan.slots[s_, b]
+            for which in range(2):
+                for h in range(c.hkv):
+                    pat = ((t * 131 + d * 7 + h * 31 + b * 13 + which * 101 + s_ * 59)
+                           % 256).astype(np.uint8)
+                    off = which * c.page_bytes() + h * sec
+                    hc.arena[slot, off:off + pay] = pat.reshape(-1)
+    codes = set()
+    for h in range(c.hkv):
+        codes |= set(np.unique(hc.arena[hc.plan.slots[0, 0], h * sec:h * sec + pay]).tolist())
+    assert codes == set(range(256))
+    dc = kvcase.DeviceCase(hc)
+    dc.out.fill_(0x7FC0)
+    got = run_v2(be, dc, split=split)
+    kvcase.assert_close_bf16(got, hc.oracle_decode(), what=f"all payload codes, split={split}")

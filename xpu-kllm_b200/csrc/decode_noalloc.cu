@@ -184,17 +184,17 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	float *part = reinterpret_cast<float *>(scratch + kCounterBytes);
 	void *list = scratch + kListOffset;
 
-	// split < 0: one warp per (seq, kv head), no scratch used (as in v2).
+	// split < 0: one warp per (seq, kv head), no partial slots (as in v2);
+	// the queue is still used to recompute MX segments exactly.
 	const int split = p->split >= 0;
-	if (split) {
-		// The counters must start at zero; the array keeps whatever the last
-		// call left, so clear the words this call uses (no allocation involved).
-		const size_t segs = (size_t)p->num_seqs * p->num_kv_heads;
-		if (cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess ||
-		    cudaMemsetAsync(list, 0, 32, st) != cudaSuccess) {
-			(void)cudaGetLastError();
-			return KLLM_EIO;
-		}
+	// The counters and the queue header must start at zero; the array keeps
+	// whatever the last call left, so clear the words this call uses (no
+	// allocation involved).
+	const size_t segs = (size_t)p->num_seqs * p->num_kv_heads;
+	if ((split && cudaMemsetAsync(cnt, 0, segs * sizeof(unsigned), st) != cudaSuccess) ||
+	    cudaMemsetAsync(list, 0, 32, st) != cudaSuccess) {
+		(void)cudaGetLastError();
+		return KLLM_EIO;
 	}
 
 	struct kllm_decode_args a;
@@ -220,7 +220,7 @@ extern "C" int kllm_gpu_paged_attention_v2_noalloc(
 	a.split = split;
 	a.ws_part = split ? part : nullptr;
 	a.ws_cnt = split ? cnt : nullptr;
-	a.ws_list = split ? list : nullptr;
+	a.ws_list = list;
 
 	const size_t row = (size_t)p->num_heads * p->head_dim;
 	for (int s0 = 0; s0 < p->num_seqs; s0 += KLLM_MAX_SEQS_LAUNCH) {

@@ -87,6 +87,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
 	return false;
 }
 
+// Programmatic dependent launch. In a kernel launched with programmatic
+// stream serialization, grid_dependency_wait() returns once the previous
+// kernel on the stream has completed and its writes are visible;
+// grid_launch_dependents() lets the next such kernel start launching. Both
+// are no-ops in a kernel launched normally.
+__device__ __forceinline__ void grid_dependency_wait()
+{
+	asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents()
+{
+	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_ns()
 {
 	uint64_t t;
@@ -225,6 +240,17 @@ __device__ __forceinline__ uint32_t mx_scale_lut_entry_f16(uint32_t code)
 			  : (float)m * __uint_as_float(116u << 23);
 	const uint32_t h = pack_f16x2(v, v);
 	return (code & 0x80u) ? (h | 0x80008000u) : h;
+}
+
+// One E4M3 code as the reference decodes it (userspace/compute/mx_dequant.h:
+// 30-55): bias 7, subnormals m/8 * 2^-6, and exponent 15 with mantissa 7
+// (0x7F / 0xFF) as +-480 rather than NaN. Exact in fp32.
+__device__ __forceinline__ float e4m3_ref_to_f32(uint32_t code)
+{
+	const uint32_t e = (code >> 3) & 0xFu, m = code & 0x7u;
+	const float v = e ? __uint_as_float(((e + 120u) << 23) | (m << 20))
+			  : (float)m * __uint_as_float(118u << 23);
+	return (code & 0x80u) ? -v : v;
 }
 
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b)

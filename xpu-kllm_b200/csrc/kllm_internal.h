@@ -21,6 +21,7 @@ extern "C" {
 #define KLLM_ERR_SEQ_TOO_LONG_BIT 0x1u /* seq_len beyond the table: clamped */
 #define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
 #define KLLM_ERR_TOPK_RANGE_BIT 0x10u /* a row asked for top-k above 1024 */
+#define KLLM_ERR_NONFINITE_BIT 0x20u /* MX payload 0x7F/0xFF not recomputed */
 /* MX-FP8 decode computes with K/V values scaled by 2^-2 (payload x scale
  * stays below the f16 maximum); scores and outputs are multiplied back. */
 #define KLLM_MX_DEC_UNBIAS   4.0f
@@ -48,13 +49,17 @@ struct kllm_decode_args {
 	void *ws_list;            /* split: merge work list (KLLM_MERGE_LIST_BYTES, header
 	                             zero between calls) or NULL: merge in the decode */
 	int total_warps;          /* warps launched (grid * KLLM_DEC_WARPS) */
+	int overlap;              /* launch as a programmatic dependent of the previous
+	                             kernel on the stream (KLLM_DECODE_OVERLAP_PREV) */
 };
 
 /* Segments split over more than KLLM_FUSED_MERGE_MAX warps are not merged by
  * the last warp of the decode but queued for kllm_decode_merge_launch, which
  * merges each (segment, query head) with a whole CTA. */
 #ifndef KLLM_FUSED_MERGE_MAX
+#ifndef KLLM_FUSED_MERGE_MAX
 #define KLLM_FUSED_MERGE_MAX   16
+#endif
 #endif
 #define KLLM_MERGE_LIST_CAP    1024
 #define KLLM_MERGE_LIST_BYTES  (32 + 24 * KLLM_MERGE_LIST_CAP)

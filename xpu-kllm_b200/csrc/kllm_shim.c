@@ -409,14 +409,16 @@ static int decode_chunk(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *a,
 	a->split = split;
 	a->ws_part = ws_part;
 	a->ws_cnt = ws_cnt;
-	a->ws_list = split ? ws_list : NULL;
+	/* the queue also carries MX segments to recompute exactly (payload codes
+	 * 0x7F / 0xFF), with or without split-KV */
+	a->ws_list = ws_list;
 	a->total_warps = grid * KLLM_DEC_WARPS;
 	int e = kllm_decode_launch(a, grid, st);
 	if (e)
 		return KLLM_EIO;
 	if (ctx)
 		ctx->stats.launches++;
-	if (split && ws_list) {
+	if (ws_list && (split || a->kv_dtype == KLLM_KV_MX_FP8_E4M3)) {
 		if (kllm_decode_merge_launch(a, num_sms, st))
 			return KLLM_EIO;
 		if (ctx)
@@ -442,11 +444,11 @@ static int decode_common(struct kllm_gpu_ctx *ctx, struct kllm_decode_args *base
 			per = (int)by_cnt;
 	}
 	void *ws_list = NULL;
-	if (split) {
-		if (ws_part_bytes < KLLM_MERGE_LIST_BYTES)
-			return KLLM_ENOSPC;
+	if (ws_part && ws_part_bytes >= KLLM_MERGE_LIST_BYTES) {
 		ws_part_bytes -= KLLM_MERGE_LIST_BYTES;
 		ws_list = (uint8_t *)ws_part + ws_part_bytes;
+	} else if (split) {
+		return KLLM_ENOSPC;
 	}
 	int max_warps = (int)(ws_part_bytes / (2ull * KLLM_SLOT_FLOATS * sizeof(float)));
 	if (split && max_warps < KLLM_DEC_WARPS)
@@ -567,7 +569,7 @@ uint64_t kllm_gpu_decode_workspace_size(struct kllm_gpu_ctx *ctx, int num_seqs,
 int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
 				const struct kllm_gpu_attention_params_v2 *p)
 {
-	if (!p || p->struct_size < sizeof(*p))
+	if (!p || p->struct_size < sizeof(*p) || (p->flags & ~KLLM_DECODE_OVERLAP_PREV))
 		return fail(ctx, KLLM_EINVAL);
 	if (!ready(ctx))
 		return fail(ctx, KLLM_ENODEV);
@@ -618,6 +620,7 @@ int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
 	a.pl = p->partial_l;
 	a.po = p->partial_o;
 	a.err = p->err_word;
+	a.overlap = (p->flags & KLLM_DECODE_OVERLAP_PREV) != 0;
 	if (partial)
 		a.out = NULL;
 	rc = decode_common(ctx, &a, split, wsp, wsp_bytes, cnt, cnt_cap,

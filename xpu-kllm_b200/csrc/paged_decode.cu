@@ -690,6 +690,34 @@ __device__ __forceinline__ void merge_segment(const kllm_decode_args &a, const S
 		merge_segment_gp<D, 1>(a, sg, seg_x0, T, W, unbias, lane);
 }
 
+// Queues segment (s, h) for the wide merge: its partials merged by a whole
+// CTA (exact = 0), or the segment recomputed there from its pages with the
+// reference's E4M3 decoding (exact = 1: a piece came out of the tile loop
+// non-finite). False when the queue is full.
+__device__ __forceinline__ bool queue_segment(const kllm_decode_args &a, int s, int h, int ts,
+					      long long seg_x0, long long T, long long W,
+					      int exact, int lane)
+{
+	ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
+	ListItem *li = reinterpret_cast<ListItem *>(lh + 1);
+	unsigned idx = 0;
+	if (lane == 0) {
+		idx = atomicAdd(&lh->count, 1u);
+		if (idx < KLLM_MERGE_LIST_CAP) {
+			li[idx].s = s;
+			li[idx].h = h;
+			li[idx].ts = ts;
+			li[idx].pad = exact;
+			li[idx].seg_x0 = seg_x0;
+			if (!exact) {
+				lh->T = T;
+				lh->W = W;
+			}
+		}
+	}
+	return __shfl_sync(0xffffffffu, idx, 0) < KLLM_MERGE_LIST_CAP;
+}
+
 template <int D, int KVT>
 __global__ void __launch_bounds__(kWarps * 32, Geom<D, KVT>::MIN_CTAS)
 decode_kernel(const kllm_decode_args a)
@@ -711,6 +739,7 @@ decode_kernel(const kllm_decode_args a)
 	if constexpr (Gm::MX)
 		for (int i = tid; i < 256; i += blockDim.x)
 			lut[i] = mx_scale_lut_entry_f16((uint32_t)i);
+	bool clamped = false;  // reported after the grid dependency wait
 	{
 		bool too_long = false;
 		const int cap = a.max_blocks * a.block_size;
@@ -723,8 +752,8 @@ decode_kernel(const kllm_decode_args a)
 			}
 			slen[s] = L;
 		}
-		if (too_long && a.err && blockIdx.x == 0)
-			atomicOr(a.err, 0x1u);
+		if (too_long && blockIdx.x == 0)
+			clamped = true;
 	}
 	if (lane == 0)
 		for (int i = 0; i < Gm::NST; ++i)
@@ -756,16 +785,26 @@ decode_kernel(const kllm_decode_args a)
 	const long long T = (long long)prefix[S] * H;
 	const int w = blockIdx.x * kWarps + warp;
 
-	for (int s = w; s < S; s += a.total_warps)
-		if (prefix[s + 1] == prefix[s])
+	if (T == 0) {
+		grid_dependency_wait();
+		if (clamped && a.err)
+			atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
+		for (int s = w; s < S; s += a.total_warps)
 			write_empty_seq<D>(a, s, lane);
-	if (T == 0)
 		return;
+	}
 
 	const long long W = a.split ? (T < a.total_warps ? T : a.total_warps)
 				    : a.total_warps;
-	if (w >= W)
+	if (w >= W) {
+		grid_dependency_wait();
+		if (clamped && a.err)
+			atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
+		for (int s = w; s < S; s += a.total_warps)
+			if (prefix[s + 1] == prefix[s])
+				write_empty_seq<D>(a, s, lane);
 		return;
+	}
 	long long xa, xb;
 	if (a.split) {
 		xa = (long long)w * T / W;
@@ -774,8 +813,15 @@ decode_kernel(const kllm_decode_args a)
 		xa = seg_start_at_or_after(prefix, S, H, T, (long long)w * T / W);
 		xb = seg_start_at_or_after(prefix, S, H, T, (long long)(w + 1) * T / W);
 	}
-	if (xa >= xb)
+	if (xa >= xb) {
+		grid_dependency_wait();
+		if (clamped && a.err)
+			atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
+		for (int s = w; s < S; s += a.total_warps)
+			if (prefix[s + 1] == prefix[s])
+				write_empty_seq<D>(a, s, lane);
 		return;
+	}
 	const int n = (int)(xb - xa);
 
 	uint8_t *wst = smem + lay.stage + (size_t)warp * Gm::NST * Gm::STAGE;
@@ -790,6 +836,22 @@ decode_kernel(const kllm_decode_args a)
 	Batch cur, nxt;
 	load_batch(cur, a, prefix, slen, xa, n, 0, lane, tpp);
 	load_batch(nxt, a, prefix, slen, xa, n, 32, lane, tpp);
+
+	// Everything above reads only seq_lens and the block table (and writes
+	// shared memory). Launched as a programmatic dependent (overlap), this
+	// CTA got here while the previous kernel on the stream was finishing;
+	// the query, the pages and every output are touched only after it has
+	// completed. The decode itself never signals its dependents early: the
+	// next kernel's CTAs, parked on the SMs its warps leave, slowed the
+	// decode's last warps (measured), so the wide merge launches when the
+	// decode completes, and signals the next decode at once.
+	grid_dependency_wait();
+	if (clamped && a.err)
+		atomicOr(a.err, KLLM_ERR_SEQ_TOO_LONG_BIT);
+	for (int s = w; s < S; s += a.total_warps)
+		if (prefix[s + 1] == prefix[s])
+			write_empty_seq<D>(a, s, lane);
+
 	finalize_batch(cur, a, sec);
 	int pb = 0;
 
@@ -911,6 +973,18 @@ decode_kernel(const kllm_decode_args a)
 		}
 		const bool full = piece_j0 == 0 && seg_end;
 		const size_t row0 = (size_t)cc.s * a.num_heads + (size_t)cc.h * a.group;
+		// MX: a non-finite piece means payload codes 0x7F / 0xFF (the
+		// hardware conversion's NaN, the reference's +-480); its segment is
+		// recomputed exactly by the wide-merge kernel, which runs after this
+		// one and overwrites what this one wrote for it
+		bool redo = false;
+		if constexpr (Gm::MX) {
+			bool bad = !isfinite(L0) || !isfinite(L1);
+#pragma unroll
+			for (int mt = 0; mt < D / 16; ++mt)
+				bad |= !isfinite(o[mt][0] + o[mt][1] + o[mt][2] + o[mt][3]);
+			redo = __any_sync(0xffffffffu, bad);
+		}
 		if (full) {
 #pragma unroll
 			for (int hp = 0; hp < 2; ++hp) {
@@ -926,6 +1000,9 @@ decode_kernel(const kllm_decode_args a)
 							  hp ? m1 : m0, hp ? L1 : L0, unbias);
 				}
 			}
+			if (redo && !(a.ws_list && queue_segment(a, cc.s, cc.h, cc.ts, 0, T, W, 1,
+								  lane)) && lane == 0 && a.err)
+				atomicOr(a.err, KLLM_ERR_NONFINITE_BIT);
 		} else {
 			const int which = piece_x0 == xa ? 0 : 1;
 			float *slot = a.ws_part + ((size_t)w * 2 + which) * KLLM_SLOT_FLOATS;
@@ -950,6 +1027,12 @@ decode_kernel(const kllm_decode_args a)
 			const long long seg_x0 = piece_x0 - piece_j0;
 			const long long npieces = owner_warp(seg_x0 + cc.ts - 1, T, W) -
 						  owner_warp(seg_x0, T, W) + 1;
+			// a segment of few pieces is merged in this kernel; one of many is
+			// queued by its last piece, and the wide merge checks its result
+			if (redo && npieces <= KLLM_FUSED_MERGE_MAX &&
+			    !(a.ws_list && queue_segment(a, cc.s, cc.h, cc.ts, seg_x0, T, W, 1, lane)) &&
+			    lane == 0 && a.err)
+				atomicOr(a.err, KLLM_ERR_NONFINITE_BIT);
 			unsigned old = 0;
 			unsigned *cnt = a.ws_cnt + (size_t)cc.s * H + cc.h;
 			if (lane == 0)
@@ -958,24 +1041,8 @@ decode_kernel(const kllm_decode_args a)
 			if ((long long)old == npieces - 1) {
 				__threadfence();
 				bool fused = npieces <= KLLM_FUSED_MERGE_MAX || !a.ws_list;
-				if (!fused) {  // long segment: queue it for the wide merge
-					ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
-					ListItem *li = reinterpret_cast<ListItem *>(lh + 1);
-					unsigned idx = 0;
-					if (lane == 0) {
-						idx = atomicAdd(&lh->count, 1u);
-						if (idx < KLLM_MERGE_LIST_CAP) {
-							li[idx].s = cc.s;
-							li[idx].h = cc.h;
-							li[idx].ts = cc.ts;
-							li[idx].seg_x0 = seg_x0;
-							lh->T = T;
-							lh->W = W;
-						}
-					}
-					idx = __shfl_sync(0xffffffffu, idx, 0);
-					fused = idx >= KLLM_MERGE_LIST_CAP;
-				}
+				if (!fused)    // long segment: queue it for the wide merge
+					fused = !queue_segment(a, cc.s, cc.h, cc.ts, seg_x0, T, W, 0, lane);
 				if (fused)
 					merge_segment<D>(a, cc, seg_x0, T, W, unbias, lane);
 				if (lane == 0)
@@ -1008,6 +1075,104 @@ decode_kernel(const kllm_decode_args a)
 	}
 }
 
+// Exact recompute of one (segment, query head) of an MX-FP8 decode by a CTA
+// of 8 warps, for segments whose tile-loop result was not finite: payload
+// codes 0x7F / 0xFF, which the hardware E4M3 conversion reads as NaN and the
+// reference decodes as +-480 (userspace/compute/mx_dequant.h:30-55). No
+// writer of either code base emits them, but pages that arrive from a store
+// are raw bytes. Warp w takes tiles w, w+8, ... of the segment, reads them
+// with plain loads and decodes every value exactly in fp32 (payload x
+// scale), lane -> D/32 dims; the warps' (m, l, o) are merged in shared
+// memory and the row is written over what the decode wrote for it.
+template <int D>
+__device__ void exact_pair(const kllm_decode_args &a, int s, int h, int hh, int ts,
+			   float (*sm_o)[D], float *sm_m, float *sm_l)
+{
+	constexpr int NV = D / 32;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int tpp = a.block_size / kTile;
+	const size_t sec = (size_t)a.block_size * D * 9 / 8;
+	// the decode's scale carries the 2^2 that undoes its V / 4
+	const float sl2 = a.scale_log2 * (1.f / KLLM_MX_DEC_UNBIAS);
+	const int cap = a.max_blocks * a.block_size;
+	int L = a.seq_lens[s];
+	L = L < 0 ? 0 : (L > cap ? cap : L);
+	const size_t row = (size_t)s * a.num_heads + (size_t)h * a.group + hh;
+	const uint16_t *qp = reinterpret_cast<const uint16_t *>(a.q) + row * D + lane * NV;
+	float q[NV], o[NV];
+#pragma unroll
+	for (int i = 0; i < NV; ++i) {
+		q[i] = __uint_as_float((uint32_t)qp[i] << 16);
+		o[i] = 0.f;
+	}
+	float m = -CUDART_INF_F, l = 0.f;
+	for (int j = warp; j < ts; j += 8) {
+		const int page = j / tpp, sub = j - page * tpp;
+		const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+				    (size_t)s * a.max_blocks + page;
+		const unsigned long long kp = e->k, vp = e->v;
+		if (!e->valid || !kp || ((kp | vp) & 15ull))
+			continue;   // skipped by the decode as well
+		const int ntok = min(L - j * kTile, kTile);
+		const uint8_t *kb = reinterpret_cast<const uint8_t *>(kp) + a.layer_off + (size_t)h * sec;
+		const uint8_t *vb = reinterpret_cast<const uint8_t *>(vp) + a.layer_off + (size_t)h * sec;
+		for (int t = 0; t < ntok; ++t) {
+			const size_t r = (size_t)sub * kTile + t;
+			const size_t so = (size_t)a.block_size * D + r * (D / 8) + lane * NV / 8;
+			const float ksc = e4m3_ref_to_f32(kb[so]), vsc = e4m3_ref_to_f32(vb[so]);
+			float dot = 0.f;
+#pragma unroll
+			for (int i = 0; i < NV; ++i)
+				dot = fmaf(q[i], e4m3_ref_to_f32(kb[r * D + lane * NV + i]) * ksc, dot);
+#pragma unroll
+			for (int off = 16; off > 0; off >>= 1)
+				dot += __shfl_xor_sync(0xffffffffu, dot, off);
+			const float x = dot * sl2;
+			const float mn = fmaxf(m, x);
+			const float f = exp2f(m - mn), pw = exp2f(x - mn);
+			l = fmaf(l, f, pw);
+#pragma unroll
+			for (int i = 0; i < NV; ++i)
+				o[i] = fmaf(o[i], f, pw * e4m3_ref_to_f32(vb[r * D + lane * NV + i]) * vsc);
+			m = mn;
+		}
+	}
+	if (lane == 0) {
+		sm_m[warp] = m;
+		sm_l[warp] = l;
+	}
+#pragma unroll
+	for (int i = 0; i < NV; ++i)
+		sm_o[warp][lane * NV + i] = o[i];
+	__syncthreads();
+	if (threadIdx.x < D) {
+		const int d = threadIdx.x;
+		float M = -CUDART_INF_F;
+#pragma unroll
+		for (int w = 0; w < 8; ++w)
+			if (sm_l[w] > 0.f)
+				M = fmaxf(M, sm_m[w]);
+		float Lt = 0.f, od = 0.f;
+#pragma unroll
+		for (int w = 0; w < 8; ++w) {
+			const float ew = sm_l[w] > 0.f ? exp2f(sm_m[w] - M) : 0.f;
+			Lt = fmaf(sm_l[w], ew, Lt);
+			od = fmaf(sm_o[w][d], ew, od);
+		}
+		const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+		if (a.pm) {
+			a.po[row * D + d] = od * inv;
+			if (d == 0) {
+				a.pm[row] = Lt > 0.f ? M * 0.69314718055994531f : -CUDART_INF_F;
+				a.pl[row] = Lt;
+			}
+		} else {
+			reinterpret_cast<__nv_bfloat16 *>(a.out)[row * D + d] = __float2bfloat16_rn(od * inv);
+		}
+	}
+	__syncthreads();
+}
+
 // Wide merge of the queued long segments: one CTA of 8 warps per
 // (segment, query head). Pass 1: the segment's maximum over all its pieces
 // (independent loads by all threads, block reduction). Pass 2: warp w sums
@@ -1023,10 +1188,16 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 	__shared__ float sm_l[8];
 	__shared__ float sm_o[8][D];
 	__shared__ int last;
+	grid_dependency_wait();     // the decode that filled the queue has completed
+	grid_launch_dependents();
 	ListHeader *lh = static_cast<ListHeader *>(a.ws_list);
 	const ListItem *li = reinterpret_cast<const ListItem *>(lh + 1);
 	const unsigned count = min(*reinterpret_cast<volatile unsigned *>(&lh->count),
 				   (unsigned)KLLM_MERGE_LIST_CAP);
+	// Nothing queued (every segment was merged inside the decode): the
+	// header is already clear, no CTA needs to count itself done.
+	if (count == 0)
+		return;
 	const long long T = lh->T, W = lh->W;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	constexpr int NV = D / 32;
@@ -1036,6 +1207,10 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 	for (long long pr = blockIdx.x; pr < pairs; pr += gridDim.x) {
 		const ListItem it = li[pr / a.group];
 		const int hh = (int)(pr % a.group);
+		if (it.pad) {   // queued for an exact recompute (MX payload 0x7F / 0xFF)
+			exact_pair<D>(a, it.s, it.h, hh, it.ts, sm_o, sm_red, sm_l);
+			continue;
+		}
 		const long long w0 = owner_warp(it.seg_x0, T, W);
 		const long long np = owner_warp(it.seg_x0 + it.ts - 1, T, W) - w0 + 1;
 		auto slot_of = [&](long long r) -> const float * {
@@ -1113,14 +1288,24 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 		for (int i = 0; i < NV; ++i)
 			sm_o[warp][lane * NV + i] = acc[i];
 		__syncthreads();
+		float Lt = 0.f, o = 0.f;
 		if (threadIdx.x < D) {
 			const int d = threadIdx.x;
-			float Lt = 0.f, o = 0.f;
 #pragma unroll
 			for (int w = 0; w < 8; ++w) {
 				Lt += sm_l[w];
 				o += sm_o[w][d];
 			}
+		}
+		// MX pieces that came out of the decode non-finite (payload 0x7F /
+		// 0xFF): recompute the segment exactly instead of writing them
+		const bool bad = threadIdx.x < D && !(isfinite(Lt) && isfinite(o));
+		if (__syncthreads_or(bad) && a.kv_dtype == 1) {   // 1: MX-FP8 pages
+			exact_pair<D>(a, it.s, it.h, hh, it.ts, sm_o, sm_red, sm_l);
+			continue;
+		}
+		if (threadIdx.x < D) {
+			const int d = threadIdx.x;
 			const size_t row = (size_t)it.s * a.num_heads + (size_t)it.h * a.group + hh;
 			const float inv = Lt > 0.f ? unbias / Lt : 0.f;
 			if (a.pm) {
@@ -1145,6 +1330,27 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 		lh->count = 0u;
 		lh->done = 0u;
 	}
+}
+
+// Launches `kernel`, as a programmatic dependent of the previous kernel on
+// the stream when `dependent` is set (it may then start while that kernel
+// finishes; its griddepcontrol.wait orders everything after it).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_maybe_dependent(void (*kernel)(KArgs...), int grid, int block,
+				   size_t smem, cudaStream_t st, int dependent,
+				   Args... args)
+{
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3((unsigned)grid);
+	cfg.blockDim = dim3((unsigned)block);
+	cfg.dynamicSmemBytes = smem;
+	cfg.stream = st;
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = dependent ? 1 : 0;
+	return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 template <int D, int KVT>
@@ -1176,8 +1382,8 @@ struct Launcher {
 		cudaError_t e = prepare(a.num_seqs);
 		if (e != cudaSuccess)
 			return e;
-		decode_kernel<D, KVT><<<grid, kWarps * 32, smem(a.num_seqs), st>>>(a);
-		return cudaGetLastError();
+		return launch_maybe_dependent(decode_kernel<D, KVT>, grid, kWarps * 32,
+					      smem(a.num_seqs), st, a.overlap, a);
 	}
 };
 
@@ -1225,18 +1431,21 @@ extern "C" int kllm_decode_preload(void)
 extern "C" int kllm_decode_merge_launch(const struct kllm_decode_args *a,
 					int num_sms, void *stream)
 {
-	if (!a->ws_list || !a->split)
+	if (!a->ws_list)
 		return 0;
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
 	const float unbias = a->kv_dtype ? KLLM_MX_DEC_UNBIAS : 1.f;
-	const int grid = num_sms > 0 ? num_sms : 148;
+	// CTAs take (segment, query head) pairs grid-stride; two per SM cover the
+	// queue of a decode split over many warps in one wave, and an empty queue
+	// costs only the launch
+	const int grid = 2 * (num_sms > 0 ? num_sms : 148);
 	if (a->head_dim == 128)
-		merge_big_kernel<128><<<grid, 256, 0, st>>>(*a, unbias);
-	else if (a->head_dim == 64)
-		merge_big_kernel<64><<<grid, 256, 0, st>>>(*a, unbias);
-	else
-		return (int)cudaErrorInvalidValue;
-	return (int)cudaGetLastError();
+		return (int)launch_maybe_dependent(merge_big_kernel<128>, grid, 256, 0, st,
+						   a->overlap, *a, unbias);
+	if (a->head_dim == 64)
+		return (int)launch_maybe_dependent(merge_big_kernel<64>, grid, 256, 0, st,
+						   a->overlap, *a, unbias);
+	return (int)cudaErrorInvalidValue;
 }
 
 extern "C" int kllm_decode_launch(const struct kllm_decode_args *a, int grid,

@@ -26,6 +26,8 @@ KV_BF16, KV_MX_FP8, KV_MX_BF16_COMPAT = 0, 1, 2
 # error codes
 OK, EIO, ENOMEM, ENODEV, EINVAL, ENOSPC, ENOSYS, ETIMEDOUT = 0, -5, -12, -19, -22, -28, -38, -110
 ERR_SEQ_TOO_LONG, ERR_MISALIGNED, ERR_APPEND_NOPAGE, ERR_TIMEOUT = 0x1, 0x2, 0x4, 0x8
+ERR_TOPK_RANGE, ERR_NONFINITE = 0x10, 0x20
+DECODE_OVERLAP_PREV = 0x1   # kllm_gpu_attention_params_v2.flags
 
 
 class AttnParams(Structure):
