@@ -878,7 +878,7 @@ def run_prefill(args) -> None:
                                 "peak": hpeak, "unit": "GB/s", "peak_kind": hkind,
                                 "frac": round(rig.append_bytes() / (ap_ms * 1e-3) / 1e9 / hpeak,
                                               4),
-                                "kernel": "append_kernel", "launch_ms": round(ap_ms, 4)},
+                                "kernel": "append_warp_kernel<128> (MX-FP8 quantize-on-write)", "launch_ms": round(ap_ms, 4)},
             "e2e": {"value": round(rig.n_tok * args.steps / (te_ms * 1e-3), 1),
                     "unit": "tokens/s",
                     "h2d_bytes_per_step": int(sum(nbytes)),

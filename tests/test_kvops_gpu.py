@@ -85,19 +85,24 @@ def _section_bytes(kv, block, d):
 
 @pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8, 2])
 @pytest.mark.parametrize("extreme", [False, True])
-def test_append_bit_exact(be, kv, extreme, random_bits=False):
+def test_append_bit_exact(be, kv, extreme, random_bits=False, block=16, d=128, hkv=8,
+                          offset=0):
     import torch
-    cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme, random_bits=random_bits)
+    cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme, random_bits=random_bits,
+                                             block=block, d=d, hkv=hkv)
     sec = _section_bytes(kv, cfg.block, cfg.d)
     page = cfg.hkv * sec
     slot_bytes = 2 * page
-    arena_h = np.zeros((plan.n_slots, slot_bytes), dtype=np.uint8)
-    arena_d = torch.zeros((plan.n_slots, slot_bytes), dtype=torch.uint8, device="cuda")
+    arena_h = np.zeros((plan.n_slots, slot_bytes + offset), dtype=np.uint8)
+    arena_d = torch.zeros((plan.n_slots, slot_bytes + offset), dtype=torch.uint8,
+                          device="cuda")
+    slot_bytes += offset   # pages offset within 16-byte alignment when offset % 16 != 0
 
     def table(base):
         t = np.zeros(plan.slots.shape, dtype=wl.ENTRY_DTYPE)
         used = plan.slots >= 0
-        addr = np.uint64(base) + plan.slots.clip(0).astype(np.uint64) * np.uint64(slot_bytes)
+        addr = np.uint64(base + offset) + plan.slots.clip(0).astype(np.uint64) * \
+            np.uint64(slot_bytes)
         t["k"] = np.where(used, addr, 0)
         t["v"] = np.where(used, addr + np.uint64(page), 0)
         t["valid"] = used
@@ -125,6 +130,21 @@ def test_append_bit_exact(be, kv, extreme, random_bits=False):
     if not np.array_equal(got, arena_h):
         diff = np.argwhere(got != arena_h)
         raise AssertionError(f"{len(diff)} bytes differ; first {diff[:5].tolist()}")
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+@pytest.mark.parametrize("block,d,hkv", [(32, 64, 4), (16, 128, 16), (64, 64, 1), (128, 128, 2)])
+def test_append_shapes_bit_exact(be, kv, block, d, hkv):
+    """Head dims 64 and 128 with 1 to 16 kv heads (16 x 128: more than one
+    pass of the warp over a token's row) and blocks of 16 to 128 tokens."""
+    test_append_bit_exact(be, kv, True, random_bits=kv == wl.KV_MX_FP8, block=block, d=d,
+                          hkv=hkv)
+
+
+def test_append_pages_8_byte_aligned(be):
+    """MX pages only 8-byte aligned: scale bytes are written one by one
+    instead of as a 16-byte row, with the same result."""
+    test_append_bit_exact(be, wl.KV_MX_FP8, False, random_bits=True, offset=8)
 
 
 @pytest.mark.parametrize("kv", [wl.KV_MX_FP8, 2])

@@ -80,6 +80,105 @@ constexpr E4m3Tables make_e4m3_tables()
 
 __device__ const E4m3Tables g_e4m3 = make_e4m3_tables();
 
+// The same values as {value, reciprocal} pairs, one 8-byte load per code.
+struct E4m3Pairs {
+	float2 p[256];
+};
+
+constexpr E4m3Pairs make_e4m3_pairs()
+{
+	E4m3Pairs t{};
+	for (int i = 0; i < 256; ++i) {
+		const float v = e4m3_value_host(i);
+		t.p[i] = float2{v, v != 0.0f ? 1.0f / v : 0.0f};
+	}
+	return t;
+}
+
+__device__ const E4m3Pairs g_e4m3_pairs = make_e4m3_pairs();
+
+// Smallest E4M3 code >= amax / 448 (amax > 0), as mx_scale_code_tab, in
+// integer and fp32 arithmetic only (no conversion unit, which the payload
+// encoding keeps busy). t = amax / 448 as in mx_scale_code_tab; E4M3 codes
+// are ordered like their values, so the code is t rounded up:
+//  * t >= 2^-6 (normal codes): the code is t's exponent and top three
+//    mantissa bits, (bits >> 20) - (120 << 3), plus one when any lower bit
+//    is set;
+//  * t < 2^-6 (subnormal codes m * 2^-9, and code 8 = 2^-6): ceil(t * 512),
+//    with t * 512 exact and rounded to an integer by the 1.5 * 2^23 addend.
+// Checked against the exact rule for every positive finite bf16 amax.
+__device__ __forceinline__ uint32_t mx_scale_code_int(float amax)
+{
+	constexpr float r448 = 1.0f / 448.0f;
+	const float q0 = amax * r448;
+	const float t = fmaf(fmaf(-448.0f, q0, amax), r448, q0);
+	if (t > 448.0f)
+		return 0x7Eu;
+	const uint32_t tb = __float_as_uint(t);
+	if (tb >= 0x3C800000u)   // 2^-6
+		return (tb >> 20) - 960u + ((tb & 0xFFFFFu) != 0u ? 1u : 0u);
+	const float y = t * 512.0f;
+	const float r = y + 12582912.0f;
+	const uint32_t n = __float_as_uint(r) - 0x4B400000u;   // round(y)
+	return n + ((r - 12582912.0f) < y ? 1u : 0u);
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: per lane the same IEEE
+// round-to-nearest operation as the scalar instruction).
+__device__ __forceinline__ unsigned long long f2_from_bf16x2(uint32_t w)
+{
+	unsigned long long r;
+	asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(w << 16), "r"(w & 0xFFFF0000u));
+	return r;
+}
+
+__device__ __forceinline__ unsigned long long f2_splat(float x)
+{
+	unsigned long long r;
+	asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(x));
+	return r;
+}
+
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b)
+{
+	unsigned long long r;
+	asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+	return r;
+}
+
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+						     unsigned long long c)
+{
+	unsigned long long r;
+	asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+	return r;
+}
+
+// Two bf16 (one word) over the E4M3 value s with y = RN(1 / s): the exact
+// quotient of append_store (reciprocal + one residual step), two lanes at a
+// time, encoded as two E4M3 codes (byte 0: the low element).
+__device__ __forceinline__ uint32_t quot_e4m3x2(uint32_t w, unsigned long long ns,
+						unsigned long long y)
+{
+	const unsigned long long f = f2_from_bf16x2(w);
+	const unsigned long long q0 = f2_mul(f, y);
+	const unsigned long long q = f2_fma(f2_fma(ns, q0, f), y, q0);
+	float lo, hi;
+	asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(q));
+	return cvt_e4m3x2(lo, hi);
+}
+
+// max |x| of eight bf16 values (four words), as a float; NaN lanes are
+// ignored like fmaxf ignores them.
+__device__ __forceinline__ float bf16x8_absmax(uint4 x)
+{
+	uint32_t m01, m23, m;
+	asm("max.bf16x2 %0, %1, %2;" : "=r"(m01) : "r"(x.x & 0x7FFF7FFFu), "r"(x.y & 0x7FFF7FFFu));
+	asm("max.bf16x2 %0, %1, %2;" : "=r"(m23) : "r"(x.z & 0x7FFF7FFFu), "r"(x.w & 0x7FFF7FFFu));
+	asm("max.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(m01), "r"(m23));
+	return fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+}
+
 // Smallest E4M3 code >= amax / 448 (the reference quantizer's scale rule,
 // mx_dequant.h:119-120, with a real E4M3 encoding in place of its stub).
 // t = amax / 448 through the correctly rounded
@@ -284,6 +383,152 @@ __global__ void __launch_bounds__(256) append_chunk_kernel(const kllm_append_arg
 	append_tokens(a, tab, i0, s_seq, s_pos);
 }
 
+// Quantize-on-write, one warp per token (head_dim 64 or 128; MX-FP8 or
+// BF16 pages). The token's K and V rows (num_kv_heads x D bf16 each, one
+// contiguous run) are loaded first, 16 bytes per lane and micro-block, so
+// the sequence and page lookup that follows runs while they are in flight;
+// lane l then owns micro-blocks l, l+32, ... (head = index / (D/8), at
+// compile-time shifts). MX: each lane writes its 8 payload bytes (16 lanes
+// cover one head's 128-byte row) and its scale byte.
+// `cu` == nullptr: token i goes to (token_seq[i], token_pos[i]); otherwise
+// token i of the chunk goes to sequence s (cu[s] <= i < cu[s+1]) at
+// position ctx[s] + i - cu[s].
+template <int D>
+__global__ void __launch_bounds__(256, 4) append_warp_kernel(const kllm_append_args a,
+							  const int *cu, const int *ctx)
+{
+	constexpr int NB = D / 8;      // micro-blocks per head row
+	constexpr int HPL = 32 / NB;   // head rows covered by one pass of the warp
+	constexpr int kU = 4;          // micro-blocks per lane held per pass
+	const int lane = threadIdx.x & 31;
+	const int i = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+	if (i >= a.num_tokens)
+		return;
+	const int H = a.num_kv_heads;
+	const int per_row = H * NB;
+	const uint4 *ksrc = reinterpret_cast<const uint4 *>(a.k) + (size_t)i * per_row;
+	const uint4 *vsrc = reinterpret_cast<const uint4 *>(a.v) + (size_t)i * per_row;
+
+	uint4 xk[kU], xv[kU];
+#pragma unroll
+	for (int u = 0; u < kU; ++u) {
+		const int mb = lane + 32 * u;
+		if (mb < per_row) {
+			xk[u] = __ldcs(ksrc + mb);
+			xv[u] = __ldcs(vsrc + mb);
+		}
+	}
+
+	// ---- token -> (sequence, position) -> page ------------------------------
+	int seq = -1, pos = -1;
+	if (!cu) {
+		seq = a.token_seq[i];
+		pos = a.token_pos[i];
+	} else {
+		// lane l looks at sequence b0 + l: its chunk start, end and cached
+		// length in one round of loads; the sequence holding row i is the
+		// lane whose chunk contains it (chunks are ordered and disjoint)
+		for (int b0 = 0; b0 < a.num_seqs; b0 += 32) {
+			const int s = b0 + lane;
+			int c0 = 0, c1 = 0, cx = 0;
+			if (s < a.num_seqs) {
+				c0 = __ldg(cu + s);
+				c1 = __ldg(cu + s + 1);
+				cx = __ldg(ctx + s);
+			}
+			const bool mine = s < a.num_seqs && c0 <= i && i < c1;
+			const unsigned hit = __ballot_sync(0xffffffffu, mine);
+			if (hit) {
+				const int src = __ffs(hit) - 1;
+				seq = b0 + src;
+				pos = __shfl_sync(0xffffffffu, cx + (i - c0), src);
+				break;
+			}
+			if (__shfl_sync(0xffffffffu, c0, 31) > i)
+				break;   // every later chunk starts after row i
+		}
+	}
+	const int bs = a.block_size;
+	const int blk = pos >= 0 ? pos / bs : -1;
+	unsigned long long kp = 0ull, vp = 0ull;
+	if (seq >= 0 && seq < a.num_seqs && blk >= 0 && blk < a.max_blocks) {
+		const DevEntry *e = reinterpret_cast<const DevEntry *>(a.table) +
+				    (size_t)seq * a.max_blocks + blk;
+		kp = e->k;
+		vp = e->v;
+		if (!e->valid || !kp || !vp)
+			kp = vp = 0ull;
+	}
+	if (!kp) {
+		if (lane == 0 && a.err)
+			atomicOr(a.err, 0x4u);
+		return;
+	}
+	kp += a.layer_off;
+	vp += a.layer_off;
+	const bool mx = a.kv_dtype == 1;
+	// payload stores are 8 (MX) or 16 (BF16) bytes wide
+	const unsigned long long need = mx ? 7ull : 15ull;
+	if ((kp | vp) & need) {
+		if (lane == 0 && a.err)
+			atomicOr(a.err, 0x2u);
+		return;
+	}
+	const int slot = pos - blk * bs;
+	const size_t sec = mx ? (size_t)bs * D * 9 / 8 : (size_t)bs * D * 2;
+	// lane -> micro-block b of head row (lane / NB) + HPL * u of each pass
+	const int b = lane % NB;
+	const size_t lane_off = (size_t)(lane / NB) * sec;
+	const size_t pay_off = mx ? (size_t)slot * D + b * 8 : ((size_t)slot * D + b * 8) * 2;
+	const size_t scl_off = (size_t)bs * D + (size_t)slot * NB;
+	const float2 *pairs = g_e4m3_pairs.p;
+
+	for (int c0 = 0; c0 < per_row; c0 += 32 * kU) {
+		if (c0) {   // more than 4 x 32 micro-blocks per row (many kv heads)
+#pragma unroll
+			for (int u = 0; u < kU; ++u) {
+				const int mb = c0 + lane + 32 * u;
+				if (mb < per_row) {
+					xk[u] = __ldcs(ksrc + mb);
+					xv[u] = __ldcs(vsrc + mb);
+				}
+			}
+		}
+		const size_t pass_off = (size_t)(c0 / NB) * sec + lane_off;
+#pragma unroll
+		for (int kv = 0; kv < 2; ++kv) {
+			uint8_t *page = reinterpret_cast<uint8_t *>(kv ? vp : kp) + pass_off;
+#pragma unroll
+			for (int u = 0; u < kU; ++u) {
+				const bool in = c0 + lane + 32 * u < per_row;
+				uint8_t *secp = page + (size_t)(HPL * u) * sec;
+				const uint4 x = kv ? xv[u] : xk[u];
+				if (!mx) {
+					if (in)
+						*reinterpret_cast<uint4 *>(secp + pay_off) = x;
+					continue;
+				}
+				const float amax = bf16x8_absmax(x);
+				uint32_t code = 0u, lo = 0u, hi = 0u;
+				if (in && amax > 0.f) {
+					code = mx_scale_code_int(amax);
+					// the exact quotient of append_store (reciprocal + residual)
+					const float2 sy = __ldg(&pairs[code]);
+					const unsigned long long ns = f2_splat(-sy.x), y = f2_splat(sy.y);
+					lo = quot_e4m3x2(x.x, ns, y) | (quot_e4m3x2(x.y, ns, y) << 16);
+					hi = quot_e4m3x2(x.z, ns, y) | (quot_e4m3x2(x.w, ns, y) << 16);
+				}
+				if (in)
+					*reinterpret_cast<uint2 *>(secp + pay_off) = make_uint2(lo, hi);
+				// one byte per lane: the NB lanes of a head row write its NB
+				// scale bytes in one store instruction
+				if (in)
+					secp[scl_off + b] = (uint8_t)code;
+			}
+		}
+	}
+}
+
 // One warp per (seq, kv head): walk the pages in order, skip invalid
 // entries, dequantise every valid token row exactly to bf16.
 __global__ void gather_kernel(const kllm_gather_args a)
@@ -392,10 +637,30 @@ static dim3 append_grid(const struct kllm_append_args *a, int threads)
 		    (unsigned)((per_token + threads - 1) / threads));
 }
 
+// Head dims 64 and 128 with MX-FP8 or BF16 pages take the warp-per-token
+// kernel; other shapes and the reference's BF16-payload layout the general one.
+static bool append_by_warp(const struct kllm_append_args *a)
+{
+	return (a->head_dim == 128 || a->head_dim == 64) && (a->kv_dtype == 0 || a->kv_dtype == 1);
+}
+
+static int append_warp_launch(const struct kllm_append_args *a, const int *cu,
+			      const int *ctx, cudaStream_t st)
+{
+	const unsigned blocks = (unsigned)((a->num_tokens + 7) / 8);
+	if (a->head_dim == 128)
+		append_warp_kernel<128><<<blocks, 256, 0, st>>>(*a, cu, ctx);
+	else
+		append_warp_kernel<64><<<blocks, 256, 0, st>>>(*a, cu, ctx);
+	return (int)cudaGetLastError();
+}
+
 extern "C" int kllm_append_launch(const struct kllm_append_args *a, void *stream)
 {
 	if (a->num_tokens <= 0)
 		return 0;
+	if (append_by_warp(a))
+		return append_warp_launch(a, nullptr, nullptr, static_cast<cudaStream_t>(stream));
 	append_kernel<<<append_grid(a, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
 	return (int)cudaGetLastError();
 }
@@ -406,6 +671,8 @@ extern "C" int kllm_append_chunk_launch(const struct kllm_append_args *a,
 {
 	if (a->num_tokens <= 0)
 		return 0;
+	if (append_by_warp(a))
+		return append_warp_launch(a, cu_seqlens, ctx_lens, static_cast<cudaStream_t>(stream));
 	append_chunk_kernel<<<append_grid(a, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
 	    *a, cu_seqlens, ctx_lens);
 	return (int)cudaGetLastError();
