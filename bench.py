@@ -41,10 +41,10 @@ METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200
 
 # DRAM bytes per decode launch / algorithmic bytes, from one ncu capture of
 # decode_kernel<128,1> on the C2 workload (64 requests, 350.9 MB algorithmic):
-# 351.9 MB read + 4.7 MB written (outputs and split-KV partials). Traffic
+# 351.95 MB read + 4.13 MB written (outputs and split-KV partials). Traffic
 # grows with the bytes processed, so a launch of B algorithmic bytes moves
 # about B x this ratio.
-DECODE_TRAFFIC_RATIO = 1.0162
+DECODE_TRAFFIC_RATIO = 1.0147
 
 # What the decode computes in, per KV format: MX-FP8 pages are dequantised in
 # registers to f16 (exact E4M3 x E4M3 products, scaled by 2^-2) and contracted
@@ -502,8 +502,11 @@ def run_kllm(args) -> None:
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind,
                          "traffic": round(per_launch_bytes * DECODE_TRAFFIC_RATIO),
-                         "traffic_source": "ncu dram__bytes_read+write of the C2 workload, "
-                                           "scaled by algorithmic bytes per launch",
+                         "traffic_source": "one ncu --set full capture of the same kernel on "
+                                           "the C2 workload: (351.95 MB read + 4.13 MB "
+                                           "written) / 350.9 MB algorithmic = 1.0147, times "
+                                           "this launch's algorithmic bytes "
+                                           "(profiles/decode_kernel_mxfp8_c2_b64.md)",
                          "kernel": "decode_kernel<128,1> (MX-FP8)"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(cfg.layers * qb + rig.B * 4),
