@@ -134,6 +134,9 @@ int kllm_gpu_paged_attention_cuda(
 #define KLLM_ERR_APPEND_NOPAGE  0x4u  /* append target page invalid / position out of table */
 #define KLLM_ERR_TIMEOUT        0x8u  /* a bounded device-side wait expired; the warp stopped */
 #define KLLM_ERR_TOPK_RANGE     0x10u /* lm_head: top_k in (1024, vocab): token -1 for that row */
+#define KLLM_ERR_PAGE_RANGE     0x40u /* a page outside every arena registered with
+                                        kllm_gpu_register_arena: skipped, never read
+                                        or written */
 #define KLLM_ERR_NONFINITE      0x20u /* decode: an MX-FP8 page holds payload 0x7F / 0xFF and the
                                         segment could not be recomputed exactly (split < 0, or
                                         the wide-merge queue was full): its rows are not finite */
@@ -380,6 +383,43 @@ struct kllm_gpu_stats {
 	int last_cuda_error;         /* cudaError_t behind the last KLLM_EIO (0: none) */
 };
 int kllm_gpu_get_stats(struct kllm_gpu_ctx *ctx, struct kllm_gpu_stats *out);
+
+/* Page range checks (no counterpart in the reference, whose kernel checks
+ * only valid / NULL, userspace/gpu/paged_attention.cu:59-60). Registers
+ * [base, base + bytes) as a KV arena of this context (up to 8). While any
+ * arena is registered, the decode, append and prefill launched through this
+ * context check every page a block-table entry names: a page (the kv head
+ * section read, or the whole page written) outside all arenas is skipped
+ * and KLLM_ERR_PAGE_RANGE is OR-ed into err_word. Nothing traps. */
+int kllm_gpu_register_arena(struct kllm_gpu_ctx *ctx, const void *base, uint64_t bytes);
+void kllm_gpu_clear_arenas(struct kllm_gpu_ctx *ctx);
+
+/* Per-call GPU timing for the tracer's GPU_SUBMIT / GPU_COMPLETE stages
+ * (bpf/kllm_trace.bpf.c:37-38, which nothing in the reference emits). With
+ * tracing enabled (kllm_gpu_trace_enable, or KLLM_GPU_TRACE=<capacity> in the
+ * environment at kllm_gpu_create), every decode, append and prefill call
+ * through the context records a CUDA event pair around its launches; the
+ * events are created when tracing is enabled, none in the call. An event
+ * between two decodes keeps the second from overlapping the first
+ * (KLLM_DECODE_OVERLAP_PREV), so tracing costs some throughput.
+ * kllm_gpu_trace_read returns completed records in call order without
+ * blocking; calls made while capacity records are unread are dropped and
+ * counted. */
+#define KLLM_TRACE_DECODE  1u
+#define KLLM_TRACE_APPEND  2u
+#define KLLM_TRACE_PREFILL 3u
+#define KLLM_TRACE_MAX     65536
+struct kllm_gpu_trace_record {
+	uint64_t seq;                /* call number since tracing was enabled */
+	uint64_t tag;                /* kllm_gpu_trace_tag at the call (e.g. request id) */
+	uint64_t submit_ns;          /* CLOCK_MONOTONIC at the call (the tracer's clock) */
+	uint32_t op;                 /* KLLM_TRACE_* */
+	float gpu_us;                /* device time of the call's kernels (-1: unknown) */
+};
+int kllm_gpu_trace_enable(struct kllm_gpu_ctx *ctx, int capacity);  /* 0: off */
+void kllm_gpu_trace_tag(struct kllm_gpu_ctx *ctx, uint64_t tag);
+int kllm_gpu_trace_read(struct kllm_gpu_ctx *ctx, struct kllm_gpu_trace_record *out,
+			int max_records, uint64_t *dropped);
 
 /* Cross-GPU split-KV exchange over NCCL (NVLink). One context per rank.
  * kllm_gpu_comm_get_unique_id runs on one rank; its 128 bytes reach the

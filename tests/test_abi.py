@@ -122,6 +122,11 @@ def test_no_device_context_fails_loudly():
         lp = kb.LmHeadParams()
         lp.struct_size = ctypes.sizeof(lp)
         assert lib.kllm_gpu_lm_head_sample(ctx, ctypes.byref(lp)) == kb.ENODEV
+        # arena bookkeeping is host-side; tracing needs a device
+        assert lib.kllm_gpu_register_arena(ctx, 4096, 1 << 20) == 0
+        lib.kllm_gpu_clear_arenas(ctx)
+        assert lib.kllm_gpu_trace_read(ctx, None, 0, None) == 0
+        assert lib.kllm_gpu_trace_enable(ctx, 8) == kb.ENODEV
         st = kb.Stats()
         assert lib.kllm_gpu_get_stats(ctx, ctypes.byref(st)) == 0
         assert st.errors >= 4 and st.last_error == kb.ENODEV

@@ -371,3 +371,85 @@ def test_mx_decode_every_payload_code(be, split):
     dc.out.fill_(0x7FC0)
     got = run_v2(be, dc, split=split)
     kvcase.assert_close_bf16(got, hc.oracle_decode(), what=f"all payload codes, split={split}")
+
+
+def test_registered_arenas_page_range_checks(be):
+    """With arenas registered, a page outside all of them is skipped by the
+    decode (KLLM_ERR_PAGE_RANGE, output as if the entry were invalid) and
+    never written by the append."""
+    import torch
+    cfg = replace(wl.C2, batch=5)
+    hc = kvcase.build_case(cfg, seq_lens=[700, 16, 1, 2049, 333])
+    c = hc.cfg
+    dc = kvcase.DeviceCase(hc)
+    lib, ctx = be.lib, be.ctx
+    n = hc.plan.n_slots
+    slot_b = c.slot_bytes()
+    base = dc.arena.data_ptr()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        # the whole arena registered: nothing changes
+        assert lib.kllm_gpu_register_arena(ctx, base, n * slot_b) == 0
+        got = run_v2(be, dc, err_word=err.data_ptr())
+        assert int(err.item()) == 0
+        kvcase.assert_close_bf16(got, hc.oracle_decode(), what="whole arena registered")
+        # only the first half of the slots registered
+        lib.kllm_gpu_clear_arenas(ctx)
+        half = n // 2
+        assert lib.kllm_gpu_register_arena(ctx, base, half * slot_b) == 0
+        got = run_v2(be, dc, err_word=err.data_ptr())
+        assert int(err.item()) & kb.ERR_PAGE_RANGE
+        ref_case = replace(hc, valid=hc.valid & (hc.plan.slots < half))
+        kvcase.assert_close_bf16(got, ref_case.oracle_decode(), what="half the arena registered")
+        # an append into an unregistered page leaves it untouched
+        before = dc.arena.clone()
+        s_out = int(np.argwhere(hc.plan.slots[0] >= half)[0][0]) if (hc.plan.slots[0] >= half).any() \
+            else None
+        if s_out is not None:
+            err.zero_()
+            kk = torch.zeros((1, c.hkv, c.d), dtype=torch.int16, device="cuda").fill_(0x3F80)
+            ts = torch.zeros(1, dtype=torch.int32, device="cuda")
+            tp = torch.full((1,), s_out * c.block, dtype=torch.int32, device="cuda")
+            rc = be.append(k=kk.data_ptr(), v=kk.data_ptr(), token_seq=ts.data_ptr(),
+                           token_pos=tp.data_ptr(), num_tokens=1, num_seqs=c.batch,
+                           block_tables=dc.table.data_ptr(), max_blocks_per_seq=hc.plan.max_blocks,
+                           num_kv_heads=c.hkv, head_dim=c.d, block_size=c.block,
+                           kv_dtype=c.kv_dtype, layer=0, layer_stride=c.layer_stride(),
+                           err_word=err.data_ptr(), stream=torch.cuda.current_stream().cuda_stream)
+            assert rc == 0
+            torch.cuda.synchronize()
+            assert int(err.item()) & kb.ERR_PAGE_RANGE
+            assert torch.equal(before, dc.arena), "an unregistered page was written"
+    finally:
+        lib.kllm_gpu_clear_arenas(ctx)
+
+
+def test_trace_records(be):
+    """Per-call GPU timing: one record per traced call, in call order, with
+    the caller's tag, the host submit time and the device time."""
+    import ctypes as ct
+    import torch
+    lib, ctx = be.lib, be.ctx
+    hc = kvcase.build_case(wl.C2, batch=8)
+    dc = kvcase.DeviceCase(hc)
+    assert lib.kllm_gpu_trace_enable(ctx, 4) == 0
+    try:
+        lib.kllm_gpu_trace_tag(ctx, 77)
+        for _ in range(6):     # two beyond the ring's capacity: dropped
+            be.decode_v2(**dc.decode_kwargs(
+                stream=torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        recs = (kb.TraceRecord * 8)()
+        dropped = ct.c_uint64(0)
+        n = lib.kllm_gpu_trace_read(ctx, recs, 8, ct.byref(dropped))
+        assert n == 4 and dropped.value == 2
+        assert [recs[i].op for i in range(n)] == [kb.TRACE_DECODE] * 4
+        assert all(recs[i].tag == 77 and recs[i].gpu_us > 0 for i in range(n))
+        assert [recs[i].seq for i in range(n)] == [0, 1, 2, 3]
+        assert all(recs[i + 1].submit_ns >= recs[i].submit_ns for i in range(n - 1))
+        # the ring has room again
+        be.decode_v2(**dc.decode_kwargs(stream=torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert lib.kllm_gpu_trace_read(ctx, recs, 8, None) == 1 and recs[0].seq == 4
+    finally:
+        assert lib.kllm_gpu_trace_enable(ctx, 0) == 0

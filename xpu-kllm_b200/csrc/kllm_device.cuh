@@ -9,6 +9,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "kllm_internal.h"
+
 namespace kllm {
 
 // ---------------------------------------------------------------------------
@@ -85,6 +87,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity)
 		if (mbar_try_wait(bar, parity))
 			return true;
 	return false;
+}
+
+// True when [p, p + bytes) lies inside one registered arena, or when no
+// arena is registered (the check is off).
+__device__ __forceinline__ bool in_arenas(const kllm_arenas &ar, unsigned long long p,
+					  unsigned long long bytes)
+{
+	if (ar.count <= 0)
+		return true;
+	bool ok = false;
+	for (int r = 0; r < ar.count && r < KLLM_MAX_ARENAS; ++r)
+		ok |= p >= ar.lo[r] && p + bytes <= ar.hi[r] && p + bytes >= p;
+	return ok;
 }
 
 // Programmatic dependent launch. In a kernel launched with programmatic

@@ -22,6 +22,16 @@ extern "C" {
 #define KLLM_ERR_TIMEOUT_BIT 0x8u /* a bounded device wait expired */
 #define KLLM_ERR_TOPK_RANGE_BIT 0x10u /* a row asked for top-k above 1024 */
 #define KLLM_ERR_NONFINITE_BIT 0x20u /* MX payload 0x7F/0xFF not recomputed */
+#define KLLM_ERR_PAGE_RANGE_BIT 0x40u /* a page outside the registered arenas: skipped */
+
+/* Device memory ranges the caller registered as KV arenas; when count > 0
+ * every page a kernel reads or writes must lie inside one of them. */
+#define KLLM_MAX_ARENAS 8
+struct kllm_arenas {
+	int count;
+	int pad;
+	unsigned long long lo[KLLM_MAX_ARENAS], hi[KLLM_MAX_ARENAS];  /* [lo, hi) */
+};
 /* MX-FP8 decode computes with K/V values scaled by 2^-2 (payload x scale
  * stays below the f16 maximum); scores and outputs are multiplied back. */
 #define KLLM_MX_DEC_UNBIAS   4.0f
@@ -51,6 +61,7 @@ struct kllm_decode_args {
 	int total_warps;          /* warps launched (grid * KLLM_DEC_WARPS) */
 	int overlap;              /* launch as a programmatic dependent of the previous
 	                             kernel on the stream (KLLM_DECODE_OVERLAP_PREV) */
+	struct kllm_arenas arenas;
 };
 
 /* Segments split over more than KLLM_FUSED_MERGE_MAX warps are not merged by
@@ -88,6 +99,7 @@ struct kllm_append_args {
 	int max_blocks, num_kv_heads, head_dim, block_size, kv_dtype;
 	uint64_t layer_off;
 	uint32_t *err;
+	struct kllm_arenas arenas;
 };
 int kllm_append_launch(const struct kllm_append_args *a, void *stream);
 
@@ -115,6 +127,7 @@ struct kllm_prefill_args {
 	uint64_t layer_off;
 	float scale_log2;
 	uint32_t *err;
+	struct kllm_arenas arenas;
 };
 int kllm_prefill_launch(const struct kllm_prefill_args *a, void *stream);
 

@@ -70,7 +70,74 @@ struct kllm_gpu_ctx {
 	uint8_t **p2p_peers_dev;                 /* the same table in device memory */
 	int p2p_max_rows, p2p_head_dim, p2p_nranks, p2p_rank;
 	unsigned p2p_epoch;
+	/* registered KV arenas (page range checks) */
+	struct kllm_arenas arenas;
+	/* per-call GPU timing: a ring of event pairs created when enabled */
+	struct trace_slot *trace;
+	int trace_cap;
+	uint64_t trace_head, trace_tail, trace_dropped, trace_tag;
 };
+
+struct trace_slot {
+	cudaEvent_t ev0, ev1;
+	uint64_t submit_ns, tag;
+	uint32_t op;
+};
+
+static uint64_t mono_ns(void)
+{
+	struct timespec ts;
+	clock_gettime(CLOCK_MONOTONIC, &ts);
+	return (uint64_t)ts.tv_sec * 1000000000ull + (uint64_t)ts.tv_nsec;
+}
+
+/* Opens a traced call on `st`: returns its ring slot, or -1 (tracing off, or
+ * the ring is full because records were not read: the call is counted as
+ * dropped). */
+static int trace_begin(struct kllm_gpu_ctx *ctx, cudaStream_t st, uint32_t op)
+{
+	if (!ctx || !ctx->trace)
+		return -1;
+	if (ctx->trace_head - ctx->trace_tail >= (uint64_t)ctx->trace_cap) {
+		ctx->trace_dropped++;
+		return -1;
+	}
+	int i = (int)(ctx->trace_head % (uint64_t)ctx->trace_cap);
+	struct trace_slot *t = &ctx->trace[i];
+	t->submit_ns = mono_ns();
+	t->tag = ctx->trace_tag;
+	t->op = op;
+	if (cudaEventRecord(t->ev0, st) != cudaSuccess) {
+		(void)cudaGetLastError();
+		return -1;
+	}
+	return i;
+}
+
+static void trace_end(struct kllm_gpu_ctx *ctx, cudaStream_t st, int i)
+{
+	if (i < 0)
+		return;
+	if (cudaEventRecord(ctx->trace[i].ev1, st) != cudaSuccess) {
+		(void)cudaGetLastError();
+		return;
+	}
+	ctx->trace_head++;
+}
+
+static void trace_free(struct kllm_gpu_ctx *ctx)
+{
+	if (!ctx->trace)
+		return;
+	for (int i = 0; i < ctx->trace_cap; i++) {
+		cudaEventDestroy(ctx->trace[i].ev0);
+		cudaEventDestroy(ctx->trace[i].ev1);
+	}
+	free(ctx->trace);
+	ctx->trace = NULL;
+	ctx->trace_cap = 0;
+	ctx->trace_head = ctx->trace_tail = 0;
+}
 
 static int fail(struct kllm_gpu_ctx *ctx, int code)
 {
@@ -177,6 +244,11 @@ struct kllm_gpu_ctx *kllm_gpu_create(void)
 	ctx->backend = KLLM_GPU_CUDA;
 	ctx->stats.device = dev;
 	ctx->stats.num_sms = ctx->num_sms;
+	{
+		const char *tr = getenv("KLLM_GPU_TRACE");
+		if (tr && atoi(tr) > 0)
+			(void)kllm_gpu_trace_enable(ctx, atoi(tr));
+	}
 	return ctx;
 
 fail_cnt:
@@ -203,6 +275,7 @@ void kllm_gpu_destroy(struct kllm_gpu_ctx *ctx)
 		cudaStreamSynchronize(ctx->stream);
 		kllm_gpu_comm_destroy(ctx);
 		kllm_gpu_p2p_destroy(ctx);
+		trace_free(ctx);
 		cudaFree(ctx->ws_part);
 		cudaFree(ctx->ws_cnt);
 		cudaStreamDestroy(ctx->stream);
@@ -621,10 +694,13 @@ int kllm_gpu_paged_attention_v2(struct kllm_gpu_ctx *ctx,
 	a.po = p->partial_o;
 	a.err = p->err_word;
 	a.overlap = (p->flags & KLLM_DECODE_OVERLAP_PREV) != 0;
+	a.arenas = ctx->arenas;
 	if (partial)
 		a.out = NULL;
-	rc = decode_common(ctx, &a, split, wsp, wsp_bytes, cnt, cnt_cap,
-			   ctx->num_sms, pick_stream(ctx, p->stream));
+	cudaStream_t st = pick_stream(ctx, p->stream);
+	int tr = trace_begin(ctx, st, KLLM_TRACE_DECODE);
+	rc = decode_common(ctx, &a, split, wsp, wsp_bytes, cnt, cnt_cap, ctx->num_sms, st);
+	trace_end(ctx, st, tr);
 	if (rc)
 		return rc == KLLM_EIO ? cuda_fail(ctx, cudaErrorLaunchFailure) : fail(ctx, rc);
 	return KLLM_OK;
@@ -670,7 +746,12 @@ int kllm_gpu_kv_append_v2(struct kllm_gpu_ctx *ctx,
 	a.kv_dtype = p->kv_dtype;
 	a.layer_off = (uint64_t)p->layer * p->layer_stride;
 	a.err = p->err_word;
-	if (kllm_append_launch(&a, pick_stream(ctx, p->stream)))
+	a.arenas = ctx->arenas;
+	cudaStream_t st = pick_stream(ctx, p->stream);
+	int tr = trace_begin(ctx, st, KLLM_TRACE_APPEND);
+	int le = kllm_append_launch(&a, st);
+	trace_end(ctx, st, tr);
+	if (le)
 		return cuda_fail(ctx, cudaErrorLaunchFailure);
 	ctx->stats.launches++;
 	return KLLM_OK;
@@ -722,9 +803,13 @@ int kllm_gpu_prefill_v2(struct kllm_gpu_ctx *ctx,
 	a.layer_off = (uint64_t)p->layer * p->layer_stride;
 	a.scale_log2 = p->scale * 1.4426950408889634f;
 	a.err = p->err_word;
+	a.arenas = ctx->arenas;
+	int tr = trace_begin(ctx, st, KLLM_TRACE_PREFILL);
 	int le = kllm_prefill_launch(&a, st);
-	if (le)
+	if (le) {
+		trace_end(ctx, st, tr);
 		return cuda_fail(ctx, (cudaError_t)le);
+	}
 	ctx->stats.launches++;
 	if (p->append) {
 		struct kllm_append_args b;
@@ -741,10 +826,14 @@ int kllm_gpu_prefill_v2(struct kllm_gpu_ctx *ctx,
 		b.kv_dtype = p->kv_dtype;
 		b.layer_off = a.layer_off;
 		b.err = p->err_word;
-		if (kllm_append_chunk_launch(&b, p->cu_seqlens, p->ctx_lens, st))
+		b.arenas = ctx->arenas;
+		if (kllm_append_chunk_launch(&b, p->cu_seqlens, p->ctx_lens, st)) {
+			trace_end(ctx, st, tr);
 			return cuda_fail(ctx, cudaErrorLaunchFailure);
+		}
 		ctx->stats.launches++;
 	}
+	trace_end(ctx, st, tr);
 	return KLLM_OK;
 }
 
@@ -1204,4 +1293,104 @@ void kllm_gpu_p2p_destroy(struct kllm_gpu_ctx *ctx)
 	ctx->p2p_peers_dev = NULL;
 	ctx->p2p_buf = NULL;
 	ctx->p2p_nranks = 0;
+}
+
+/* ---- registered arenas ------------------------------------------------------ */
+
+int kllm_gpu_register_arena(struct kllm_gpu_ctx *ctx, const void *base, uint64_t bytes)
+{
+	if (!ctx)
+		return KLLM_EINVAL;
+	if (!base || !bytes || (uint64_t)(uintptr_t)base + bytes < (uint64_t)(uintptr_t)base)
+		return fail(ctx, KLLM_EINVAL);
+	if (ctx->arenas.count >= KLLM_MAX_ARENAS)
+		return fail(ctx, KLLM_ENOSPC);
+	int n = ctx->arenas.count;
+	ctx->arenas.lo[n] = (unsigned long long)(uintptr_t)base;
+	ctx->arenas.hi[n] = (unsigned long long)(uintptr_t)base + bytes;
+	ctx->arenas.count = n + 1;
+	return KLLM_OK;
+}
+
+void kllm_gpu_clear_arenas(struct kllm_gpu_ctx *ctx)
+{
+	if (ctx)
+		memset(&ctx->arenas, 0, sizeof(ctx->arenas));
+}
+
+/* ---- per-call GPU timing ----------------------------------------------------- */
+
+int kllm_gpu_trace_enable(struct kllm_gpu_ctx *ctx, int capacity)
+{
+	if (!ctx || capacity < 0 || capacity > KLLM_TRACE_MAX)
+		return fail(ctx, KLLM_EINVAL);
+	if (!ready(ctx))
+		return fail(ctx, KLLM_ENODEV);
+	if (cudaSetDevice(ctx->device) != cudaSuccess)
+		return cuda_fail(ctx, cudaGetLastError());
+	/* records still queued are dropped with the old ring */
+	if (ctx->trace) {
+		cudaStreamSynchronize(ctx->stream);
+		trace_free(ctx);
+	}
+	if (capacity == 0)
+		return KLLM_OK;
+	struct trace_slot *t = calloc((size_t)capacity, sizeof(*t));
+	if (!t)
+		return fail(ctx, KLLM_ENOMEM);
+	for (int i = 0; i < capacity; i++) {
+		if (cudaEventCreate(&t[i].ev0) != cudaSuccess ||
+		    cudaEventCreate(&t[i].ev1) != cudaSuccess) {
+			(void)cudaGetLastError();
+			for (int k = 0; k <= i; k++) {
+				if (t[k].ev0)
+					cudaEventDestroy(t[k].ev0);
+				if (t[k].ev1)
+					cudaEventDestroy(t[k].ev1);
+			}
+			free(t);
+			return fail(ctx, KLLM_ENOMEM);
+		}
+	}
+	ctx->trace = t;
+	ctx->trace_cap = capacity;
+	ctx->trace_head = ctx->trace_tail = ctx->trace_dropped = 0;
+	return KLLM_OK;
+}
+
+void kllm_gpu_trace_tag(struct kllm_gpu_ctx *ctx, uint64_t tag)
+{
+	if (ctx)
+		ctx->trace_tag = tag;
+}
+
+int kllm_gpu_trace_read(struct kllm_gpu_ctx *ctx, struct kllm_gpu_trace_record *out,
+			int max_records, uint64_t *dropped)
+{
+	if (!ctx || (!out && max_records > 0) || max_records < 0)
+		return KLLM_EINVAL;
+	if (dropped)
+		*dropped = ctx->trace_dropped;
+	if (!ctx->trace)
+		return 0;
+	int n = 0;
+	while (n < max_records && ctx->trace_tail < ctx->trace_head) {
+		struct trace_slot *t = &ctx->trace[ctx->trace_tail % (uint64_t)ctx->trace_cap];
+		cudaError_t q = cudaEventQuery(t->ev1);
+		if (q == cudaErrorNotReady)
+			break;                   /* in order: later calls are not done either */
+		float ms = 0.f;
+		if (q != cudaSuccess || cudaEventElapsedTime(&ms, t->ev0, t->ev1) != cudaSuccess) {
+			(void)cudaGetLastError();
+			ms = -1.f;
+		}
+		out[n].seq = ctx->trace_tail;
+		out[n].tag = t->tag;
+		out[n].submit_ns = t->submit_ns;
+		out[n].op = t->op;
+		out[n].gpu_us = ms < 0.f ? -1.f : ms * 1000.f;
+		n++;
+		ctx->trace_tail++;
+	}
+	return n;
 }

@@ -297,6 +297,12 @@ __device__ __forceinline__ unsigned long long append_page(const kllm_append_args
 	const unsigned long long base = kv ? e->v : e->k;
 	if (!e->valid || !e->k || !base)
 		return 0ull;
+	if (!in_arenas(a.arenas, base + a.layer_off,
+		       (unsigned long long)a.num_kv_heads * section_bytes(a.kv_dtype, bs, a.head_dim))) {
+		if (a.err)   // outside the registered arenas: never written
+			atomicOr(a.err, KLLM_ERR_PAGE_RANGE_BIT);
+		return 0ull;
+	}
 	slot = pos - blk * bs;
 	return base + a.layer_off;
 }
@@ -467,6 +473,17 @@ __global__ void __launch_bounds__(256, 4) append_warp_kernel(const kllm_append_a
 	kp += a.layer_off;
 	vp += a.layer_off;
 	const bool mx = a.kv_dtype == 1;
+	{
+		// registered arenas: a page outside them is never written
+		const unsigned long long pb = (unsigned long long)H *
+					      (mx ? (size_t)a.block_size * D * 9 / 8
+						  : (size_t)a.block_size * D * 2);
+		if (!(in_arenas(a.arenas, kp, pb) && in_arenas(a.arenas, vp, pb))) {
+			if (lane == 0 && a.err)
+				atomicOr(a.err, KLLM_ERR_PAGE_RANGE_BIT);
+			return;
+		}
+	}
 	// payload stores are 8 (MX) or 16 (BF16) bytes wide
 	const unsigned long long need = mx ? 7ull : 15ull;
 	if ((kp | vp) & need) {

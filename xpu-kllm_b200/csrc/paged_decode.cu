@@ -212,8 +212,14 @@ __device__ __forceinline__ void finalize_batch(Batch &b, const kllm_decode_args 
 	const bool aligned = ((b.k | b.v) & 15ull) == 0ull;
 	if (present && !aligned && a.err)
 		atomicOr(a.err, 0x2u);
-	const bool ok = present && aligned && ntok > 0;
+	bool ok = present && aligned && ntok > 0;
 	const unsigned long long off = a.layer_off + (unsigned long long)h * sec;
+	// registered arenas: a section outside them is skipped, never read
+	if (ok && !(in_arenas(a.arenas, b.k + off, sec) && in_arenas(a.arenas, b.v + off, sec))) {
+		ok = false;
+		if (a.err)
+			atomicOr(a.err, KLLM_ERR_PAGE_RANGE_BIT);
+	}
 	b.k += off;
 	b.v += off;
 	b.pack = (ok ? ntok : 0) | (sub << 8);

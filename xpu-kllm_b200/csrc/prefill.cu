@@ -129,8 +129,13 @@ __device__ __forceinline__ const uint8_t *cached_section(const kllm_prefill_args
 	if (!e->valid || !kp)
 		return nullptr;
 	const size_t sec = a.kv_dtype == 1 ? (size_t)bs * kD * 9 / 8 : (size_t)bs * kD * 2;
-	return reinterpret_cast<const uint8_t *>(which ? vp : kp) + a.layer_off +
-	       (size_t)kvh * sec;
+	const unsigned long long p = (which ? vp : kp) + a.layer_off + (size_t)kvh * sec;
+	if (!in_arenas(a.arenas, p, sec)) {   // outside the registered arenas: skipped
+		if (a.err)
+			atomicOr(a.err, KLLM_ERR_PAGE_RANGE_BIT);
+		return nullptr;
+	}
+	return reinterpret_cast<const uint8_t *>(p);
 }
 
 // 64 MX elements (4 x 16 payload bytes, 8 scale bytes) -> 64 exact bf16

@@ -26,7 +26,14 @@ KV_BF16, KV_MX_FP8, KV_MX_BF16_COMPAT = 0, 1, 2
 # error codes
 OK, EIO, ENOMEM, ENODEV, EINVAL, ENOSPC, ENOSYS, ETIMEDOUT = 0, -5, -12, -19, -22, -28, -38, -110
 ERR_SEQ_TOO_LONG, ERR_MISALIGNED, ERR_APPEND_NOPAGE, ERR_TIMEOUT = 0x1, 0x2, 0x4, 0x8
-ERR_TOPK_RANGE, ERR_NONFINITE = 0x10, 0x20
+ERR_TOPK_RANGE, ERR_NONFINITE, ERR_PAGE_RANGE = 0x10, 0x20, 0x40
+TRACE_DECODE, TRACE_APPEND, TRACE_PREFILL = 1, 2, 3
+
+
+class TraceRecord(Structure):
+    """struct kllm_gpu_trace_record"""
+    _fields_ = [("seq", c_uint64), ("tag", c_uint64), ("submit_ns", c_uint64),
+                ("op", c_uint32), ("gpu_us", c_float)]
 DECODE_OVERLAP_PREV = 0x1   # kllm_gpu_attention_params_v2.flags
 
 
@@ -161,6 +168,11 @@ _SIGNATURES = [
     ("kllm_gpu_host_free", None, [c_void_p, c_void_p]),
     ("kllm_gpu_synchronize", c_int, [c_void_p, c_int]),
     ("kllm_gpu_get_stats", c_int, [c_void_p, POINTER(Stats)]),
+    ("kllm_gpu_register_arena", c_int, [c_void_p, c_void_p, c_uint64]),
+    ("kllm_gpu_clear_arenas", None, [c_void_p]),
+    ("kllm_gpu_trace_enable", c_int, [c_void_p, c_int]),
+    ("kllm_gpu_trace_tag", None, [c_void_p, c_uint64]),
+    ("kllm_gpu_trace_read", c_int, [c_void_p, c_void_p, c_int, POINTER(c_uint64)]),
     ("kllm_gpu_comm_get_unique_id", c_int, [POINTER(c_uint8)]),
     ("kllm_gpu_comm_init", c_int, [c_void_p, c_int, c_int, POINTER(c_uint8), c_int]),
     ("kllm_gpu_comm_merge", c_int,
