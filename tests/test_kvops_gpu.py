@@ -46,8 +46,22 @@ def _random_bits_bf16(shape, seed):
     return bits.astype(np.uint16)
 
 
+# micro-blocks with infinities and NaNs (bf16 bits): an infinity among
+# finite values, a NaN among finite values, infinities only, NaNs only (both
+# signs, quiet and signalling: abs-max 0, so the block is zero), NaN with
+# infinity, and a NaN beside values that quantize to subnormal codes
+_NONFINITE_BLOCKS = [
+    [0x7F80, 0x3F80, 0x4000, 0x4040, 0xC080, 0x40A0, 0x40C0, 0x40E0],
+    [0x7FC0, 0x3F80, 0xC000, 0x3F00, 0x0000, 0x8000, 0x0000, 0x3F80],
+    [0xFF80, 0xFF80, 0x7F80, 0x0000, 0x0000, 0x0000, 0x0000, 0x0000],
+    [0x7FC0, 0xFFC0, 0x7F81, 0xFF81, 0x7FC0, 0x7FC0, 0xFFC0, 0x7FFF],
+    [0x7FC0, 0x7F80, 0xFFC0, 0x4040, 0x0000, 0xC040, 0x0000, 0x3F80],
+    [0xFFC0, 0x3C00, 0xBC00, 0x3B80, 0x0000, 0x3A00, 0x0000, 0x3C80],
+]
+
+
 def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False,
-                 random_bits=False):
+                 random_bits=False, nonfinite=False):
     """Random tokens appended at scattered positions of a few sequences."""
     cfg = replace(wl.C1, kv_dtype=kv if kv != 2 else wl.KV_BF16, block=block, d=d, hkv=hkv,
                   hq=hkv, arena_slots=None)
@@ -71,7 +85,13 @@ def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False,
         kf[3, 0, :8] = np.array([448, -448, 447, 449, 0.001, -0.002, 464, 480])
         kf[4, 0, :8] = -0.0
         kf[5, 0, :8] = np.array([1.0, 1 / 64, 1 / 512, 1 / 1024, 1 / 700, 3 / 1024, 0, -1])
+        kf[6, 0, :8] = np.array([-0.0, 1, -0.0, 2, 0, -3, -0.0, 4])  # signed zeros kept
         k = wl.f32_to_bf16(kf)
+    if nonfinite:
+        k, v = k.copy(), v.copy()
+        for t, blk in enumerate(_NONFINITE_BLOCKS):
+            k[t, 0, :8] = blk
+            v[t + 1, hkv - 1, d - 8:] = blk
     return cfg, plan, seq, pos, k, v
 
 
@@ -86,10 +106,10 @@ def _section_bytes(kv, block, d):
 @pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8, 2])
 @pytest.mark.parametrize("extreme", [False, True])
 def test_append_bit_exact(be, kv, extreme, random_bits=False, block=16, d=128, hkv=8,
-                          offset=0):
+                          offset=0, nonfinite=False):
     import torch
     cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme, random_bits=random_bits,
-                                             block=block, d=d, hkv=hkv)
+                                             block=block, d=d, hkv=hkv, nonfinite=nonfinite)
     sec = _section_bytes(kv, cfg.block, cfg.d)
     page = cfg.hkv * sec
     slot_bytes = 2 * page
@@ -139,6 +159,15 @@ def test_append_shapes_bit_exact(be, kv, block, d, hkv):
     pass of the warp over a token's row) and blocks of 16 to 128 tokens."""
     test_append_bit_exact(be, kv, True, random_bits=kv == wl.KV_MX_FP8, block=block, d=d,
                           hkv=hkv)
+
+
+@pytest.mark.parametrize("d", [128, 64, 32])
+def test_append_nonfinite_bit_exact(be, d):
+    """Infinities and NaNs in K and V (head dims 128 and 64: the warp kernel;
+    32: the general kernel) are quantized as the oracle does: NaNs left out
+    of the abs-max, an infinite abs-max saturating the scale at 0x7E, NaN
+    and infinite elements encoded as S.1111.111 and S.1111.110."""
+    test_append_bit_exact(be, wl.KV_MX_FP8, False, random_bits=True, d=d, nonfinite=True)
 
 
 def test_append_pages_8_byte_aligned(be):

@@ -97,31 +97,48 @@ constexpr E4m3Pairs make_e4m3_pairs()
 
 __device__ const E4m3Pairs g_e4m3_pairs = make_e4m3_pairs();
 
-// Smallest E4M3 code >= amax / 448 (amax > 0), as mx_scale_code_tab, in
-// integer and fp32 arithmetic only (no conversion unit, which the payload
-// encoding keeps busy). t = amax / 448 as in mx_scale_code_tab; E4M3 codes
-// are ordered like their values, so the code is t rounded up:
-//  * t >= 2^-6 (normal codes): the code is t's exponent and top three
-//    mantissa bits, (bits >> 20) - (120 << 3), plus one when any lower bit
-//    is set;
-//  * t < 2^-6 (subnormal codes m * 2^-9, and code 8 = 2^-6): ceil(t * 512),
-//    with t * 512 exact and rounded to an integer by the 1.5 * 2^23 addend.
-// Checked against the exact rule for every positive finite bf16 amax.
-__device__ __forceinline__ uint32_t mx_scale_code_int(float amax)
+// Scale rows by the bits of a block's bf16 abs-max. Row i stands for amax =
+// bf16 bits kScaleRowLo + i (0.875 .. 200704): the smallest E4M3 code whose
+// value v satisfies 448 v >= amax (mx_dequant.h:119-120's scale, rounded up
+// to an E4M3 value), with v and -RN(1 / v). Every amax below 0.875 takes
+// code 1 (2^-9) and every one above 200704 saturates at 0x7E (448), so a
+// clamped index covers each positive finite amax.
+constexpr int kScaleRowLo = 0x3F60, kScaleRowHi = 0x4844;
+constexpr int kScaleRows = kScaleRowHi - kScaleRowLo + 1;
+
+struct ScaleRow {
+	float s, neg_y;
+	uint32_t code, pad;
+};
+struct ScaleRows {
+	ScaleRow r[kScaleRows];
+};
+
+constexpr double bf16_value_host(int bits)
 {
-	constexpr float r448 = 1.0f / 448.0f;
-	const float q0 = amax * r448;
-	const float t = fmaf(fmaf(-448.0f, q0, amax), r448, q0);
-	if (t > 448.0f)
-		return 0x7Eu;
-	const uint32_t tb = __float_as_uint(t);
-	if (tb >= 0x3C800000u)   // 2^-6
-		return (tb >> 20) - 960u + ((tb & 0xFFFFFu) != 0u ? 1u : 0u);
-	const float y = t * 512.0f;
-	const float r = y + 12582912.0f;
-	const uint32_t n = __float_as_uint(r) - 0x4B400000u;   // round(y)
-	return n + ((r - 12582912.0f) < y ? 1u : 0u);
+	const int e = (bits >> 7) & 0xFF, m = bits & 0x7F;
+	double v = e ? 128 + m : m;
+	const int ex = e ? e - 134 : -133;
+	for (int i = 0; i < (ex < 0 ? -ex : ex); ++i)
+		v = ex < 0 ? v * 0.5 : v * 2.0;
+	return v;
 }
+
+constexpr ScaleRows make_scale_rows()
+{
+	ScaleRows t{};
+	int c = 1;
+	for (int i = 0; i < kScaleRows; ++i) {
+		const double amax = bf16_value_host(kScaleRowLo + i);
+		while (448.0 * (double)e4m3_value_host(c) < amax)   // both exact in double
+			++c;
+		const float v = e4m3_value_host(c);
+		t.r[i] = ScaleRow{v, -(1.0f / v), (uint32_t)c, 0u};
+	}
+	return t;
+}
+
+__device__ const ScaleRows g_scale_rows = make_scale_rows();
 
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: per lane the same IEEE
 // round-to-nearest operation as the scalar instruction).
@@ -154,29 +171,92 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
 	return r;
 }
 
-// Two bf16 (one word) over the E4M3 value s with y = RN(1 / s): the exact
-// quotient of append_store (reciprocal + one residual step), two lanes at a
-// time, encoded as two E4M3 codes (byte 0: the low element).
-__device__ __forceinline__ uint32_t quot_e4m3x2(uint32_t w, unsigned long long ns,
-						unsigned long long y)
+// Two bf16 f (one word) over the E4M3 value s, with ny = -RN(1 / s): the
+// exact quotient of append_store (reciprocal + one residual step), two lanes
+// at a time, computed negated so that a zero keeps its sign: m = -RN(f y),
+// r = RN(f + s m) (the residual), w = RN(m - r y) = -q. Encoded as the two
+// E4M3 codes of q (byte 0: the low element), the sign bits flipped back.
+__device__ __forceinline__ uint32_t quot_e4m3x2(uint32_t w, unsigned long long s,
+						unsigned long long ny)
 {
 	const unsigned long long f = f2_from_bf16x2(w);
-	const unsigned long long q0 = f2_mul(f, y);
-	const unsigned long long q = f2_fma(f2_fma(ns, q0, f), y, q0);
+	const unsigned long long m = f2_mul(f, ny);
+	const unsigned long long nq = f2_fma(f2_fma(s, m, f), ny, m);
 	float lo, hi;
-	asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(q));
-	return cvt_e4m3x2(lo, hi);
+	asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(nq));
+	return cvt_e4m3x2(lo, hi) ^ 0x8080u;
 }
 
-// max |x| of eight bf16 values (four words), as a float; NaN lanes are
-// ignored like fmaxf ignores them.
-__device__ __forceinline__ float bf16x8_absmax(uint4 x)
+// max |x| of eight bf16 values as a float, NaN when any of them is NaN.
+__device__ __forceinline__ float bf16x8_absmax_nan(uint4 x)
 {
 	uint32_t m01, m23, m;
-	asm("max.bf16x2 %0, %1, %2;" : "=r"(m01) : "r"(x.x & 0x7FFF7FFFu), "r"(x.y & 0x7FFF7FFFu));
-	asm("max.bf16x2 %0, %1, %2;" : "=r"(m23) : "r"(x.z & 0x7FFF7FFFu), "r"(x.w & 0x7FFF7FFFu));
-	asm("max.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(m01), "r"(m23));
-	return fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+	asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(m01) : "r"(x.x & 0x7FFF7FFFu), "r"(x.y & 0x7FFF7FFFu));
+	asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(m23) : "r"(x.z & 0x7FFF7FFFu), "r"(x.w & 0x7FFF7FFFu));
+	asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(m01), "r"(m23));
+	float r;
+	asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(m << 16)),
+	    "f"(__uint_as_float(m & 0xFFFF0000u)));
+	return r;
+}
+
+// Scale row of a positive finite abs-max (a bf16 value).
+__device__ __forceinline__ uint4 scale_row(float amax)
+{
+	int idx = (int)(__float_as_uint(amax) >> 16) - kScaleRowLo;
+	idx = min(max(idx, 0), kScaleRows - 1);
+	return __ldg(reinterpret_cast<const uint4 *>(&g_scale_rows.r[idx]));
+}
+
+// A micro-block with an infinite or NaN element, quantized as the oracle's
+// restatement of the format does it: NaN elements are left out of the
+// abs-max; an infinite abs-max saturates the scale code at 0x7E (448); a
+// NaN element encodes as S.1111.111 and an infinite one as S.1111.110
+// (+-448), S its sign; a block whose abs-max is 0 is all zero. Returns the
+// scale code; lo / hi get the payload bytes (byte 0: element 0).
+__device__ __forceinline__ uint32_t mx_quantize_nonfinite(uint4 x, uint32_t &lo, uint32_t &hi)
+{
+	const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+	float amax = 0.f;
+#pragma unroll
+	for (int k = 0; k < 8; ++k) {
+		const float a = fabsf(k & 1 ? bf16hi(w[k >> 1]) : bf16lo(w[k >> 1]));
+		if (a > amax)   // false for NaN
+			amax = a;
+	}
+	lo = hi = 0u;
+	if (!(amax > 0.f))
+		return 0u;
+	float sv, ny;
+	uint32_t code;
+	if (amax <= 3.40282347e38f) {
+		const uint4 r = scale_row(amax);
+		sv = __uint_as_float(r.x);
+		ny = __uint_as_float(r.y);
+		code = r.z;
+	} else {
+		const float2 sy = __ldg(&g_e4m3_pairs.p[0x7E]);
+		sv = sy.x;
+		ny = -sy.y;
+		code = 0x7Eu;
+	}
+	uint32_t b[8];
+#pragma unroll
+	for (int k = 0; k < 8; ++k) {
+		const float f = k & 1 ? bf16hi(w[k >> 1]) : bf16lo(w[k >> 1]);
+		const uint32_t sign = (__float_as_uint(f) >> 31) << 7;
+		if (isnan(f)) {
+			b[k] = sign | 0x7Fu;
+		} else if (isinf(f)) {
+			b[k] = sign | 0x7Eu;
+		} else {   // the negated quotient of quot_e4m3x2
+			const float m = f * ny;
+			b[k] = (cvt_e4m3x2(fmaf(fmaf(sv, m, f), ny, m), 0.f) & 0xFFu) ^ 0x80u;
+		}
+	}
+	lo = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+	hi = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+	return code;
 }
 
 // Smallest E4M3 code >= amax / 448 (the reference quantizer's scale rule,
@@ -221,27 +301,32 @@ __device__ __forceinline__ void append_store(const kllm_append_args &a, const fl
 		amax = fmaxf(amax, fabsf(f[k]));
 
 	if (a.kv_dtype == 1) {
-		const uint32_t code = mx_scale_code_tab(amax, tab);
-		uint32_t lo = 0u, hi = 0u;
-		if (code != 0u) {
+		uint32_t code = 0u, lo = 0u, hi = 0u;
+		const bool finite = bf16x8_absmax_nan(x) <= 3.40282347e38f;   // false for inf / NaN
+		if (!finite)
+			code = mx_quantize_nonfinite(x, lo, hi);
+		else
+			code = mx_scale_code_tab(amax, tab);
+		if (code != 0u && finite) {
 			// x / s through the correctly rounded reciprocal plus one residual
 			// step (Markstein): exact whenever the quotient is representable,
 			// within one fp32 ulp otherwise. A bf16 x over an E4M3 s is either
 			// such an exact quotient or at least 2^-9 (relative) away from every
 			// E4M3 rounding midpoint, so the E4M3 rounding below equals that of
 			// the correctly rounded quotient.
+			// (computed negated, as quot_e4m3x2, so that a zero keeps its sign)
 			const float s = __ldg(&tab[code]);
-			const float y = __ldg(&tab[256 + code]);
-			float q[8];
+			const float ny = -__ldg(&tab[256 + code]);
+			float nq[8];
 #pragma unroll
 			for (int k = 0; k < 8; ++k) {
-				const float q0 = f[k] * y;
-				q[k] = fmaf(fmaf(-s, q0, f[k]), y, q0);
+				const float m = f[k] * ny;
+				nq[k] = fmaf(fmaf(s, m, f[k]), ny, m);
 			}
 			uint32_t p[4];
 #pragma unroll
 			for (int k = 0; k < 4; ++k)
-				p[k] = cvt_e4m3x2(q[2 * k], q[2 * k + 1]);
+				p[k] = cvt_e4m3x2(nq[2 * k], nq[2 * k + 1]) ^ 0x8080u;
 			lo = p[0] | (p[1] << 16);
 			hi = p[2] | (p[3] << 16);
 		}
@@ -389,6 +474,33 @@ __global__ void __launch_bounds__(256) append_chunk_kernel(const kllm_append_arg
 	append_tokens(a, tab, i0, s_seq, s_pos);
 }
 
+// The MX micro-blocks of token i that hold an infinite or NaN element, at
+// `slot` of the pages kp / vp (the rest of the token is already stored).
+template <int D>
+__device__ __noinline__ void append_token_nonfinite(const void *k, const void *v, int i,
+						    int num_kv_heads, int block_size,
+						    unsigned long long kp, unsigned long long vp,
+						    int slot, int lane)
+{
+	constexpr int NB = D / 8;
+	const int per_row = num_kv_heads * NB;
+	const size_t sec = (size_t)block_size * D * 9 / 8;
+	for (int kv = 0; kv < 2; ++kv) {
+		const uint4 *src = reinterpret_cast<const uint4 *>(kv ? v : k) + (size_t)i * per_row;
+		for (int mb = lane; mb < per_row; mb += 32) {
+			const uint4 x = __ldg(src + mb);
+			if (bf16x8_absmax_nan(x) <= 3.40282347e38f)
+				continue;
+			uint8_t *secp = reinterpret_cast<uint8_t *>(kv ? vp : kp) + (size_t)(mb / NB) * sec;
+			const int b = mb % NB;
+			uint32_t lo, hi;
+			const uint32_t code = mx_quantize_nonfinite(x, lo, hi);
+			*reinterpret_cast<uint2 *>(secp + (size_t)slot * D + b * 8) = make_uint2(lo, hi);
+			secp[(size_t)block_size * D + (size_t)slot * NB + b] = (uint8_t)code;
+		}
+	}
+}
+
 // Quantize-on-write, one warp per token (head_dim 64 or 128; MX-FP8 or
 // BF16 pages). The token's K and V rows (num_kv_heads x D bf16 each, one
 // contiguous run) are loaded first, 16 bytes per lane and micro-block, so
@@ -498,7 +610,7 @@ __global__ void __launch_bounds__(256, 4) append_warp_kernel(const kllm_append_a
 	const size_t lane_off = (size_t)(lane / NB) * sec;
 	const size_t pay_off = mx ? (size_t)slot * D + b * 8 : ((size_t)slot * D + b * 8) * 2;
 	const size_t scl_off = (size_t)bs * D + (size_t)slot * NB;
-	const float2 *pairs = g_e4m3_pairs.p;
+	bool nonfinite = false;
 
 	for (int c0 = 0; c0 < per_row; c0 += 32 * kU) {
 		if (c0) {   // more than 4 x 32 micro-blocks per row (many kv heads)
@@ -525,15 +637,20 @@ __global__ void __launch_bounds__(256, 4) append_warp_kernel(const kllm_append_a
 						*reinterpret_cast<uint4 *>(secp + pay_off) = x;
 					continue;
 				}
-				const float amax = bf16x8_absmax(x);
+				const float amax = bf16x8_absmax_nan(x);
 				uint32_t code = 0u, lo = 0u, hi = 0u;
-				if (in && amax > 0.f) {
-					code = mx_scale_code_int(amax);
+				if (in && amax > 0.f && amax <= 3.40282347e38f) {
+					// every element finite (a NaN fails both compares)
+					const uint4 r = scale_row(amax);
+					code = r.z;
 					// the exact quotient of append_store (reciprocal + residual)
-					const float2 sy = __ldg(&pairs[code]);
-					const unsigned long long ns = f2_splat(-sy.x), y = f2_splat(sy.y);
-					lo = quot_e4m3x2(x.x, ns, y) | (quot_e4m3x2(x.y, ns, y) << 16);
-					hi = quot_e4m3x2(x.z, ns, y) | (quot_e4m3x2(x.w, ns, y) << 16);
+					const unsigned long long sv = f2_splat(__uint_as_float(r.x));
+					const unsigned long long ny = f2_splat(__uint_as_float(r.y));
+					lo = quot_e4m3x2(x.x, sv, ny) | (quot_e4m3x2(x.y, sv, ny) << 16);
+					hi = quot_e4m3x2(x.z, sv, ny) | (quot_e4m3x2(x.w, sv, ny) << 16);
+				} else if (in && !(amax <= 3.40282347e38f)) {
+					nonfinite = true;
+					continue;
 				}
 				if (in)
 					*reinterpret_cast<uint2 *>(secp + pay_off) = make_uint2(lo, hi);
@@ -544,6 +661,10 @@ __global__ void __launch_bounds__(256, 4) append_warp_kernel(const kllm_append_a
 			}
 		}
 	}
+	// rare: micro-blocks holding an infinite or NaN element were skipped
+	// above and are quantized out of line, so the loop keeps no extra state
+	if (__any_sync(0xffffffffu, nonfinite))
+		append_token_nonfinite<D>(a.k, a.v, i, H, bs, kp, vp, slot, lane);
 }
 
 // One warp per (seq, kv head): walk the pages in order, skip invalid
