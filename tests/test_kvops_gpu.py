@@ -61,11 +61,11 @@ _NONFINITE_BLOCKS = [
 
 
 def _append_case(kv, block=16, d=128, hkv=8, seed=3, n_seq=5, extreme=False,
-                 random_bits=False, nonfinite=False):
+                 random_bits=False, nonfinite=False, lens=None):
     """Random tokens appended at scattered positions of a few sequences."""
     cfg = replace(wl.C1, kv_dtype=kv if kv != 2 else wl.KV_BF16, block=block, d=d, hkv=hkv,
                   hq=hkv, arena_slots=None)
-    lens = np.array([33, 70, 16, 1, 129][:n_seq], dtype=np.int32)
+    lens = np.array([33, 70, 16, 1, 129][:n_seq] if lens is None else lens, dtype=np.int32)
     plan = wl.plan_pages(cfg, lens, seed)
     pos = np.concatenate([np.arange(L) for L in lens]).astype(np.int32)
     seq = np.concatenate([np.full(L, s) for s, L in enumerate(lens)]).astype(np.int32)
@@ -106,10 +106,11 @@ def _section_bytes(kv, block, d):
 @pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8, 2])
 @pytest.mark.parametrize("extreme", [False, True])
 def test_append_bit_exact(be, kv, extreme, random_bits=False, block=16, d=128, hkv=8,
-                          offset=0, nonfinite=False):
+                          offset=0, nonfinite=False, lens=None):
     import torch
     cfg, plan, seq, pos, k, v = _append_case(kv, extreme=extreme, random_bits=random_bits,
-                                             block=block, d=d, hkv=hkv, nonfinite=nonfinite)
+                                             block=block, d=d, hkv=hkv, nonfinite=nonfinite,
+                                             lens=lens)
     sec = _section_bytes(kv, cfg.block, cfg.d)
     page = cfg.hkv * sec
     slot_bytes = 2 * page
@@ -168,6 +169,14 @@ def test_append_nonfinite_bit_exact(be, d):
     of the abs-max, an infinite abs-max saturating the scale at 0x7E, NaN
     and infinite elements encoded as S.1111.111 and S.1111.110."""
     test_append_bit_exact(be, wl.KV_MX_FP8, False, random_bits=True, d=d, nonfinite=True)
+
+
+@pytest.mark.parametrize("kv", [wl.KV_BF16, wl.KV_MX_FP8])
+def test_append_many_tokens_bit_exact(be, kv):
+    """More tokens (24,576, scattered over 12 sequences) than the grid has
+    warps, so each warp quantizes several."""
+    test_append_bit_exact(be, kv, True, random_bits=kv == wl.KV_MX_FP8, nonfinite=True,
+                          lens=[4096, 1, 2047, 3000, 17, 4500, 2048, 2049, 600, 3000, 1200, 2018])
 
 
 def test_append_pages_8_byte_aligned(be):

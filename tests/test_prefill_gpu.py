@@ -153,8 +153,14 @@ def test_prefill_c5_shared_prefix_sampled(be):
     rows = sorted(set(rng.integers(0, int(cu[-1]), 48).tolist()) |
                   {0, int(cu[1]) - 1, int(cu[4]), int(cu[4]) + 127, int(cu[-1]) - 1})
     want = _oracle_rows(hc, ctx_lens, cu, q, k, v, rows=rows)
-    got, _ = _run(be, *case)
+    got, arena = _run(be, *case)
     _check(got, want, "C5")
+    # the chunk's 28,672 tokens appended on write, byte for byte
+    tok_seq = np.repeat(np.arange(len(ctx_lens)), chunk_lens).astype(np.int32)
+    tok_pos = np.concatenate([np.arange(c0, c0 + n) for c0, n in zip(ctx_lens, chunk_lens)])
+    oracle.kv_append(k, v, tok_seq, tok_pos.astype(np.int32), hc.host_table(),
+                     hc.plan.max_blocks, cfg.hkv, cfg.d, cfg.block, cfg.kv_dtype)
+    assert np.array_equal(arena, hc.arena), "C5 append differs from the oracle"
 
 
 @pytest.mark.parametrize("kv", [wl.KV_MX_FP8, wl.KV_BF16])
