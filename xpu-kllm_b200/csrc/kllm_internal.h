@@ -13,7 +13,9 @@
 extern "C" {
 #endif
 
+#ifndef KLLM_DEC_WARPS
 #define KLLM_DEC_WARPS      4     /* warps per decode CTA */
+#endif
 #define KLLM_MAX_GROUP      8     /* query heads per kv head (mma N) */
 #define KLLM_SLOT_FLOATS    1040  /* one split-KV partial: o[8][128], m[8], l[8] */
 #define KLLM_MAX_SEQS_LAUNCH 4096 /* sequences per decode launch (smem prefix) */

@@ -1224,26 +1224,10 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 			const int which = (r == 0 && wr * T / W != it.seg_x0) ? 1 : 0;
 			return a.ws_part + ((size_t)wr * 2 + which) * KLLM_SLOT_FLOATS;
 		};
-		// ---- pass 1: segment maximum (log2 domain) over pieces with mass -----
-		float mx = -CUDART_INF_F;
-		for (long long r = threadIdx.x; r < np; r += blockDim.x) {
-			const float *sl = slot_of(r);
-			const float lr = __ldcg(sl + kSlotL + hh), mr = __ldcg(sl + kSlotM + hh);
-			if (lr > 0.f)
-				mx = fmaxf(mx, mr);
-		}
-#pragma unroll
-		for (int off = 16; off > 0; off >>= 1)
-			mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-		if (lane == 0)
-			sm_red[warp] = mx;
-		__syncthreads();
-		float Mt = sm_red[0];
-#pragma unroll
-		for (int w = 1; w < 8; ++w)
-			Mt = fmaxf(Mt, sm_red[w]);
-		// ---- pass 2: weighted sums against Mt, 4 pieces in flight per warp -----
-		float L = 0.f, acc[NV];
+		// ---- one pass: each warp folds its pieces (eight in flight) into a
+		// running (max, sum, o) triple in the log2 domain, rescaled whenever
+		// a batch raises its maximum; the CTA then combines the warps' triples
+		float Mw = -CUDART_INF_F, L = 0.f, acc[NV];
 #pragma unroll
 		for (int i = 0; i < NV; ++i)
 			acc[i] = 0.f;
@@ -1253,7 +1237,7 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 			for (int u = 0; u < kFly; ++u) {
 				const long long r = r0 + 8 * u;
 				lr[u] = 0.f;
-				mr[u] = 0.f;
+				mr[u] = -CUDART_INF_F;
 #pragma unroll
 				for (int i = 0; i < NV; ++i)
 					ov[u][i] = 0.f;
@@ -1277,30 +1261,52 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 					}
 				}
 			}
+			// the batch's maximum over pieces with mass (the same in every
+			// lane: all lanes read the same m and l of a piece)
+			float mb = -CUDART_INF_F;
+#pragma unroll
+			for (int u = 0; u < kFly; ++u)
+				if (lr[u] > 0.f)
+					mb = fmaxf(mb, mr[u]);
+			if (mb > Mw) {
+				const float f = exp2f(Mw - mb);   // 0 while Mw is -inf
+				L *= f;
+#pragma unroll
+				for (int i = 0; i < NV; ++i)
+					acc[i] *= f;
+				Mw = mb;
+			}
 #pragma unroll
 			for (int u = 0; u < kFly; ++u) {
 				// a piece's o is unnormalised (relative to its own max m): it
-				// weighs exp2(m - Mt); its l weighs the same into L
-				const float e = lr[u] > 0.f ? exp2f(mr[u] - Mt) : 0.f;
+				// weighs exp2(m - Mw); its l weighs the same into L
+				const float e = lr[u] > 0.f ? exp2f(mr[u] - Mw) : 0.f;
 				L = fmaf(lr[u], e, L);
 #pragma unroll
 				for (int i = 0; i < NV; ++i)
 					acc[i] = fmaf(ov[u][i], e, acc[i]);
 			}
 		}
-		if (lane == 0)
+		if (lane == 0) {
+			sm_red[warp] = Mw;
 			sm_l[warp] = L;
+		}
 #pragma unroll
 		for (int i = 0; i < NV; ++i)
 			sm_o[warp][lane * NV + i] = acc[i];
 		__syncthreads();
+		float Mt = sm_red[0];
+#pragma unroll
+		for (int w = 1; w < 8; ++w)
+			Mt = fmaxf(Mt, sm_red[w]);
 		float Lt = 0.f, o = 0.f;
 		if (threadIdx.x < D) {
 			const int d = threadIdx.x;
 #pragma unroll
 			for (int w = 0; w < 8; ++w) {
-				Lt += sm_l[w];
-				o += sm_o[w][d];
+				const float f = sm_red[w] > -CUDART_INF_F ? exp2f(sm_red[w] - Mt) : 0.f;
+				Lt = fmaf(sm_l[w], f, Lt);
+				o = fmaf(sm_o[w][d], f, o);
 			}
 		}
 		// MX pieces that came out of the decode non-finite (payload 0x7F /
