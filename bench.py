@@ -25,6 +25,7 @@ import json
 import math
 import os
 import statistics
+import select
 import subprocess
 import sys
 import time
@@ -63,16 +64,51 @@ def peaks() -> tuple[float, str]:
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clock and clock-event-reason samples during the timed region: NVML
+    read every 10 ms from a thread (so that regions of a few milliseconds
+    still get samples), else nvidia-smi every 100 ms."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period: float = 0.01):
         self.index = index
+        self.period = period
         self.proc = None
+        self.thread = None
+
+    def _nvml_start(self) -> bool:
+        try:
+            import threading
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return False
+        self.samples, self.stop_ev = [], threading.Event()
+
+        def run():
+            while True:
+                try:
+                    self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                         mx, int(reasons(h))))
+                except Exception:
+                    pass
+                if self.stop_ev.wait(self.period):
+                    break
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        return True
 
     def start(self):
+        if self._nvml_start():
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
@@ -80,8 +116,24 @@ class Clocks:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        # wait (up to 3 s) for the first sample, so that the sampler is
+        # running when the timed region starts; that sample is taken before
+        # the region and is not counted
+        ready, _, _ = select.select([self.proc.stdout], [], [], 3.0)
+        if ready:
+            self.proc.stdout.readline()
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            sm = [float(x[0]) for x in self.samples]
+            mx = [float(x[1]) for x in self.samples]
+            reasons = {nm for x in self.samples for nm, bit in self.BITS.items() if x[2] & bit}
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                    "samples": len(sm), "source": "nvml, 10 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -104,7 +156,7 @@ class Clocks:
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 100 ms"}
 
 
 # ---------------------------------------------------------------------------
