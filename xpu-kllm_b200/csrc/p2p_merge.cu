@@ -94,6 +94,10 @@ p2p_merge_kernel(const kllm_p2p_args a)
 		s_ok = ok;
 	}
 	__syncthreads();
+	// launched as a programmatic dependent of the kernel that wrote the
+	// triples: everything above ran while it finished; from here on its
+	// writes are complete and visible
+	grid_dependency_wait();
 	if (!s_ok) {
 		if (threadIdx.x == 0 && a.err)
 			atomicOr(a.err, KLLM_ERR_TIMEOUT_BIT);
@@ -197,13 +201,21 @@ extern "C" int kllm_p2p_grid(int num_rows)
 
 extern "C" int kllm_p2p_merge_launch(const struct kllm_p2p_args *a, void *stream)
 {
-	const dim3 grid(kllm_p2p_grid(a->num_rows)), block(kWarpsPerCta * 32);
-	cudaStream_t st = static_cast<cudaStream_t>(stream);
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3((unsigned)kllm_p2p_grid(a->num_rows));
+	cfg.blockDim = dim3(kWarpsPerCta * 32);
+	cfg.stream = static_cast<cudaStream_t>(stream);
+	// programmatic dependent of the previous kernel on the stream (the one
+	// that wrote m, l, o): the slot-reuse wait overlaps its end, and
+	// griddepcontrol.wait orders every read of the triples after it
+	cudaLaunchAttribute at[1];
+	at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	at[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = at;
+	cfg.numAttrs = 1;
 	if (a->head_dim == 128)
-		p2p_merge_kernel<128><<<grid, block, 0, st>>>(*a);
-	else if (a->head_dim == 64)
-		p2p_merge_kernel<64><<<grid, block, 0, st>>>(*a);
-	else
-		return (int)cudaErrorInvalidValue;
-	return (int)cudaGetLastError();
+		return (int)cudaLaunchKernelEx(&cfg, p2p_merge_kernel<128>, *a);
+	if (a->head_dim == 64)
+		return (int)cudaLaunchKernelEx(&cfg, p2p_merge_kernel<64>, *a);
+	return (int)cudaErrorInvalidValue;
 }
