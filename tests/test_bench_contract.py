@@ -58,3 +58,37 @@ def test_reference_arm_unavailable_lines():
     for cfg in ("w3_kv_arrival_4096x36k", "l3_lm_head_llama3-8b_b256_greedy"):
         line = _run("--impl", "reference", "--config", cfg)
         assert line["impl"] == "reference" and line["unavailable"]
+
+
+def test_clock_sampler_reads_nvml_during_the_region(monkeypatch):
+    """The bench's clock record comes from NVML samples taken every 10 ms on
+    a thread (checked here against a fake NVML: the median SM clock, the
+    maximum, and the clock-event reason bits mapped to their names)."""
+    import time
+    import types
+    sys.path.insert(0, ROOT)
+    import bench
+
+    calls = {"n": 0}
+    fake = types.ModuleType("pynvml")
+    fake.NVML_CLOCK_SM = 1
+    fake.nvmlInit = lambda: None
+    fake.nvmlDeviceGetHandleByIndex = lambda i: ("gpu", i)
+    fake.nvmlDeviceGetMaxClockInfo = lambda h, kind: 1965
+
+    def clock(h, kind):
+        calls["n"] += 1
+        return 1965 if calls["n"] % 2 else 1755
+
+    fake.nvmlDeviceGetClockInfo = clock
+    fake.nvmlDeviceGetCurrentClocksEventReasons = lambda h: 0x4 | 0x20   # power cap, sw thermal
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    c = bench.Clocks(3)
+    c.start()
+    time.sleep(0.08)
+    r = c.stop()
+    assert r["samples"] >= 3, r
+    assert r["sm_max_mhz"] == 1965.0
+    assert 1755.0 <= r["sm_mhz"] <= 1965.0
+    assert r["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
+    assert r["source"].startswith("nvml")
