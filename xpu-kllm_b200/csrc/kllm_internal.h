@@ -70,9 +70,7 @@ struct kllm_decode_args {
  * the last warp of the decode but queued for kllm_decode_merge_launch, which
  * merges each (segment, query head) with a whole CTA. */
 #ifndef KLLM_FUSED_MERGE_MAX
-#ifndef KLLM_FUSED_MERGE_MAX
 #define KLLM_FUSED_MERGE_MAX   16
-#endif
 #endif
 #define KLLM_MERGE_LIST_CAP    1024
 #define KLLM_MERGE_LIST_BYTES  (32 + 24 * KLLM_MERGE_LIST_CAP)
