@@ -40,12 +40,12 @@ from kllm_b200 import workloads as wl  # noqa: E402
 
 METRIC = "paged-attn decode KV GB/s (% of 8 TB/s HBM) & tokens/s at 1/2/4/8 B200"
 
-# DRAM bytes per decode launch / algorithmic bytes, from one ncu capture of
-# decode_kernel<128,1> on the C2 workload (64 requests, 350.9 MB algorithmic):
-# 351.95 MB read + 4.13 MB written (outputs and split-KV partials). Traffic
-# grows with the bytes processed, so a launch of B algorithmic bytes moves
-# about B x this ratio.
-DECODE_TRAFFIC_RATIO = 1.0147
+# DRAM bytes per decode launch / algorithmic bytes, from an ncu capture of
+# two decode_kernel<128,1> launches of the C3 workload itself (every launch
+# covers the full 256-request batch of one layer, 1.8273 GB algorithmic):
+# 1,830.7 + 4.9 MB and 1,830.6 + 2.6 MB read + written. Other decode
+# workloads scale it by the bytes they process.
+DECODE_TRAFFIC_RATIO = 1.0038
 
 # What the decode computes in, per KV format: MX-FP8 pages are dequantised in
 # registers to f16 (exact E4M3 x E4M3 products, scaled by 2^-2) and contracted
@@ -554,11 +554,12 @@ def run_kllm(args) -> None:
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind,
                          "traffic": round(per_launch_bytes * DECODE_TRAFFIC_RATIO),
-                         "traffic_source": "one ncu --set full capture of the same kernel on "
-                                           "the C2 workload: (351.95 MB read + 4.13 MB "
-                                           "written) / 350.9 MB algorithmic = 1.0147, times "
-                                           "this launch's algorithmic bytes "
-                                           "(profiles/decode_kernel_mxfp8_c2_b64.md)",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                           "of two C3 decode launches (--layers 2): mean "
+                                           "1,834.4 MB per launch against 1,827.3 MB "
+                                           "algorithmic = 1.0038, times this launch's "
+                                           "algorithmic bytes "
+                                           "(profiles/launch_list_c3_decode_bench.md)",
                          "kernel": "decode_kernel<128,1> (MX-FP8)"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(cfg.layers * qb + rig.B * 4),
