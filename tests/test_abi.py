@@ -137,7 +137,9 @@ def test_no_device_context_fails_loudly():
     assert lib.kllm_gpu_table_workspace_size(4, 8, 16) == 4 * (8 * 16 // 16 + 1) * 32
     assert lib.kllm_gpu_table_workspace_size(3, 5, 24) == 3 * (5 * 24 // 16 + 1) * 32
     assert lib.kllm_gpu_table_workspace_size(-1, 8, 16) == 0
-    assert lib.kllm_gpu_lm_head_workspace_size(256, 128256) == 256 * 501 * 12 + 32
+    # a (max, sum, argmax) partial per row and 256-row vocabulary tile, twice
+    # (the second halves of tiles computed as two halves)
+    assert lib.kllm_gpu_lm_head_workspace_size(256, 128256) == 256 * 501 * 24 + 32
     assert lib.kllm_gpu_lm_head_workspace_size(0, 128256) == 0
     # the stateless v1 launcher validates before touching a device
     assert lib.kllm_gpu_paged_attention_cuda(None, None, None, None, 1, 32, 8, 96, 4,

@@ -90,8 +90,12 @@ def _cum_ok(lg, tok, t, r):
 
 
 @pytest.mark.parametrize("R,H,V", [(1, 64, 1000), (5, 256, 1003), (128, 512, 2048),
-                                   (129, 512, 4099), (256, 1024, 8192)])
+                                   (129, 512, 4099), (256, 1024, 8192), (4, 256, 128256),
+                                   (3, 128, 21000)])
 def test_logits_and_greedy(be, R, H, V):
+    """On 148 SMs: small vocabularies run every tile as two halves; 128,256
+    rows (501 tiles) split only the last wave's 57; 21,000 rows (83 tiles)
+    split none."""
     h, w = _case(R, H, V, R * 7 + V)
     logits, tok = _run(be, h, w, None, np.zeros(R), np.zeros(R), np.zeros(R))
     _check_logits(h, w, logits, np.random.default_rng(V))
@@ -109,7 +113,7 @@ def test_greedy_ties_take_the_first_index(be):
         assert tok[r] == int(np.argmax(logits[r]))
 
 
-@pytest.mark.parametrize("R,H,V", [(16, 512, 5000), (200, 1024, 20000)])
+@pytest.mark.parametrize("R,H,V", [(16, 512, 5000), (200, 1024, 20000), (12, 256, 128256)])
 def test_temperature_and_top_k(be, R, H, V):
     rng = np.random.default_rng(V)
     h, w = _case(R, H, V, 5 + R, dup=True)

@@ -198,9 +198,13 @@ struct kllm_lm_head_args {
 	const int *top_k;         /* [num_rows] or NULL */
 	const float *uniform;     /* [num_rows] or NULL */
 	int *tokens;              /* [num_rows] */
-	float *part_m, *part_s;   /* [num_rows][tiles] */
-	int *part_a;              /* [num_rows][tiles] */
+	float *part_m, *part_s;   /* [num_rows][2 x tiles] */
+	int *part_a;              /* [num_rows][2 x tiles] */
 	uint32_t *err;
+	/* set by kllm_lm_head_launch: tiles 0..n_full-1 are computed whole,
+	 * the last n_split as two 128-row halves (the second half's partial
+	 * in slot tiles + i until the sampler folds it in) */
+	int n_full, n_split;
 };
 int kllm_lm_head_tiles(int vocab);
 int kllm_lm_head_launch(const struct kllm_lm_head_args *a, void *stream);

@@ -942,7 +942,7 @@ uint64_t kllm_gpu_lm_head_workspace_size(int num_rows, int vocab)
 {
 	if (num_rows <= 0 || vocab <= 0)
 		return 0;
-	return (uint64_t)num_rows * (uint64_t)kllm_lm_head_tiles(vocab) * 12u + 32u;
+	return (uint64_t)num_rows * (uint64_t)kllm_lm_head_tiles(vocab) * 24u + 32u;
 }
 
 int kllm_gpu_lm_head_sample(struct kllm_gpu_ctx *ctx, const struct kllm_gpu_lm_head_params *p)
@@ -960,7 +960,9 @@ int kllm_gpu_lm_head_sample(struct kllm_gpu_ctx *ctx, const struct kllm_gpu_lm_h
 		return fail(ctx, KLLM_EINVAL);
 	if (p->workspace_bytes < kllm_gpu_lm_head_workspace_size(p->num_rows, p->vocab))
 		return fail(ctx, KLLM_ENOSPC);
-	const uint64_t tiles = (uint64_t)kllm_lm_head_tiles(p->vocab) * (uint64_t)p->num_rows;
+	/* per row: a partial (max, sum, argmax) for every 256-row vocabulary
+	 * tile, plus room for the second halves of tiles split in two */
+	const uint64_t tiles = 2u * (uint64_t)kllm_lm_head_tiles(p->vocab) * (uint64_t)p->num_rows;
 	struct kllm_lm_head_args a;
 	memset(&a, 0, sizeof(a));
 	a.hidden = p->hidden;

@@ -81,7 +81,7 @@ __device__ bool lm_wait(LmSmem<MH> &sm, uint64_t *bar, uint32_t parity, uint32_t
 template <int MH>
 __global__ void __launch_bounds__(kLmThreads, 1)
 lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm_h,
-	       const __grid_constant__ CUtensorMap tm_w)
+	       const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2)
 {
 	using Sm = LmSmem<MH>;
 	constexpr int S = Sm::S;
@@ -90,9 +90,20 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 	Sm &sm = *reinterpret_cast<Sm *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
 					 ~(uintptr_t)1023);
 	const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-	const int tile = blockIdx.x, n0 = tile * kVN;
+	// CTAs 0..n_full-1 take a whole 256-row vocabulary tile; the rest take
+	// one 128-row half of one of the last n_split tiles each, so that the
+	// grid's last wave holds twice as many CTAs of half the work. The
+	// second half's partial goes to slot NT + i; the sampler folds it in.
+	const int NT = a.n_full + a.n_split;
+	const int b = blockIdx.x;
+	const bool whole = b < a.n_full;
+	const int part = whole ? 0 : (b - a.n_full) & 1;
+	const int tile = whole ? b : a.n_full + ((b - a.n_full) >> 1);
+	const int nn = whole ? kVN : kVN / 2;                   // vocabulary rows (MMA N)
+	const int n0 = tile * kVN + part * (kVN / 2);
+	const int slot = part ? NT + (tile - a.n_full) : tile;
+	const size_t stride = (size_t)NT + a.n_split;           // partial slots per row
 	const int KT = a.hidden_dim / kKt;
-	const int NT = gridDim.x;
 
 	if (tid == 0) {
 		for (int s = 0; s < S; ++s) {
@@ -125,11 +136,11 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 				const int st = kt % S, fill = kt / S;
 				if (fill > 0 && !lm_wait(sm, &sm.empty[st], (uint32_t)((fill - 1) & 1), a.err))
 					break;
-				mbar_arrive_expect_tx(&sm.full[st], MH * kABytes + kBBytes);
+				mbar_arrive_expect_tx(&sm.full[st], MH * kABytes + nn * kKt * 2);
 #pragma unroll
 				for (int h = 0; h < MH; ++h)
 					tma_load_2d(sm.a[st][h], &tm_h, kt * kKt, h * kMR, &sm.full[st]);
-				tma_load_2d(sm.b[st], &tm_w, kt * kKt, n0, &sm.full[st]);
+				tma_load_2d(sm.b[st], whole ? &tm_w : &tm_w2, kt * kKt, n0, &sm.full[st]);
 				issued[st] = fill;
 			}
 			// after an abort, wait (bounded) for this CTA's own tensor copies
@@ -142,7 +153,7 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 	} else if (warp == 1) {
 		// ================= MMA issue ================================================
 		const bool leader = elect_one();
-		const uint32_t idesc = umma_idesc_bf16(kMR, kVN, false);
+		const uint32_t idesc = umma_idesc_bf16(kMR, nn, false);
 		bool ok = true;
 		for (int kt = 0; kt < KT; ++kt) {
 			const int st = kt % S;
@@ -195,7 +206,7 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 				float m = -CUDART_INF_F, ssum = 0.f;
 				int am = -1;
 #pragma unroll 1
-				for (int c = 0; c < kVN / 32; ++c) {
+				for (int c = 0; c < nn / 32; ++c) {
 					float v[32];
 					tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kVN + c * 32), v);
 					const int nb = n0 + c * 32;
@@ -235,7 +246,7 @@ lm_head_kernel(const kllm_lm_head_args a, const __grid_constant__ CUtensorMap tm
 					}
 				}
 				if (live) {
-					const size_t p = (size_t)row * NT + tile;
+					const size_t p = (size_t)row * stride + slot;
 					a.part_m[p] = m;
 					a.part_s[p] = ssum;
 					a.part_a[p] = am;
@@ -621,7 +632,8 @@ __device__ int top_k_token(const kllm_lm_head_args &a, int row, int k, float T, 
 	const float *lg = a.logits + (size_t)row * a.vocab;
 	const int V = a.vocab;
 	const int NT = (V + kVN - 1) / kVN;
-	const int nc = tile_bound_candidates(lg, V, a.part_m + (size_t)row * NT, NT, k, sm);
+	const int nc = tile_bound_candidates(lg, V, a.part_m + (size_t)row * (NT + a.n_split), NT,
+					     k, sm);
 	if (nc >= 0) {
 		// the candidates hold the k largest: sort them all, keep the first k
 		int P = 1;
@@ -770,11 +782,36 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const kllm_lm_head
 	__shared__ SampleSmem sm;
 	const int row = blockIdx.x;
 	const int NT = (a.vocab + kVN - 1) / kVN;
-	const float *pm = a.part_m + (size_t)row * NT;
-	const float *ps = a.part_s + (size_t)row * NT;
-	const int *pa = a.part_a + (size_t)row * NT;
+	const size_t stride = (size_t)NT + a.n_split;   // partial slots per row
+	float *pm = a.part_m + (size_t)row * stride;
+	float *ps = a.part_s + (size_t)row * stride;
+	int *pa = a.part_a + (size_t)row * stride;
 	const int method = a.method ? a.method[row] : KLLM_SAMPLE_GREEDY_I;
 	const float T = a.temperature ? a.temperature[row] : 0.f;
+	// tiles computed as two halves: fold the second half (slot NT + i) into
+	// the tile's partial, as one pass over the whole tile would have left
+	// it (the larger maximum, the first half's index on equal maxima, the
+	// sums rescaled to the common maximum)
+	{
+		const float inv_t = T > 0.f ? 1.f / T : 0.f;
+		for (int i = threadIdx.x; i < a.n_split; i += kSampThreads) {
+			const int t = a.n_full + i;
+			const float m0 = pm[t], m1 = pm[NT + i];
+			const float M = fmaxf(m0, m1);
+			float sum = 0.f;
+			if (M > -CUDART_INF_F) {
+				if (m0 > -CUDART_INF_F)
+					sum += ps[t] * expf((m0 - M) * inv_t);
+				if (m1 > -CUDART_INF_F)
+					sum += ps[NT + i] * expf((m1 - M) * inv_t);
+			}
+			if (m1 > m0)
+				pa[t] = pa[NT + i];
+			pm[t] = M;
+			ps[t] = sum;
+		}
+		__syncthreads();
+	}
 	const int k = a.top_k ? a.top_k[row] : 0;
 	const float r = a.uniform ? a.uniform[row] : 0.f;
 	int tok;
@@ -795,16 +832,32 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const kllm_lm_head
 
 template <int MH>
 int launch_mh(const kllm_lm_head_args &a, const CUtensorMap &mh, const CUtensorMap &mw,
-	      cudaStream_t st)
+	      const CUtensorMap &mw2, cudaStream_t st)
 {
 	const size_t smem = sizeof(LmSmem<MH>) + 1024;
 	cudaError_t e = cudaFuncSetAttribute(lm_head_kernel<MH>,
 					     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 	if (e != cudaSuccess)
 		return (int)e;
-	const int NT = (a.vocab + kVN - 1) / kVN;
-	lm_head_kernel<MH><<<NT, kLmThreads, smem, st>>>(a, mh, mw);
+	lm_head_kernel<MH><<<a.n_full + 2 * a.n_split, kLmThreads, smem, st>>>(a, mh, mw, mw2);
 	return (int)cudaGetLastError();
+}
+
+// SMs of the current device, queried once per device (0 on error).
+int device_sms()
+{
+	static int cache[16];
+	int dev = 0;
+	if (cudaGetDevice(&dev) != cudaSuccess || dev < 0)
+		return 0;
+	if (dev < 16 && cache[dev] > 0)
+		return cache[dev];
+	int n = 0;
+	if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+		return 0;
+	if (dev < 16)
+		cache[dev] = n;
+	return n;
 }
 
 // [rows][hidden] bf16, box 64 x box_rows, 128-byte swizzle, zero fill past rows
@@ -837,14 +890,25 @@ extern "C" int kllm_lm_head_launch(const struct kllm_lm_head_args *a, void *stre
 {
 	if (a->num_rows < 1 || a->num_rows > 2 * kMR || a->hidden_dim % kKt || a->vocab < 1)
 		return (int)cudaErrorInvalidValue;
-	CUtensorMap mh, mw;
+	CUtensorMap mh, mw, mw2;
 	if (!make_rows_map(&mh, a->hidden, a->num_rows, a->hidden_dim, kMR) ||
-	    !make_rows_map(&mw, a->weight, a->vocab, a->hidden_dim, kVN))
+	    !make_rows_map(&mw, a->weight, a->vocab, a->hidden_dim, kVN) ||
+	    !make_rows_map(&mw2, a->weight, a->vocab, a->hidden_dim, kVN / 2))
 		return (int)cudaErrorInvalidValue;
+	// One CTA per SM (all of TMEM, ~197 KB of shared memory), each tile the
+	// same work: a last wave of r < SMs tiles leaves SMs idle for a whole
+	// tile. When 2r CTAs still fit in one wave, those r tiles are computed
+	// as 2r halves, so the last wave takes half as long.
+	kllm_lm_head_args b = *a;
+	const int NT = (a->vocab + kVN - 1) / kVN, sms = device_sms();
+	const int r = sms > 0 ? NT % sms : 0;
+	b.n_split = (r > 0 && 2 * r <= sms) ? r : 0;
+	b.n_full = NT - b.n_split;
 	cudaStream_t st = static_cast<cudaStream_t>(stream);
-	int rc = a->num_rows > kMR ? launch_mh<2>(*a, mh, mw, st) : launch_mh<1>(*a, mh, mw, st);
+	int rc = a->num_rows > kMR ? launch_mh<2>(b, mh, mw, mw2, st)
+				   : launch_mh<1>(b, mh, mw, mw2, st);
 	if (rc)
 		return rc;
-	sample_kernel<<<a->num_rows, kSampThreads, 0, st>>>(*a);
+	sample_kernel<<<a->num_rows, kSampThreads, 0, st>>>(b);
 	return (int)cudaGetLastError();
 }
