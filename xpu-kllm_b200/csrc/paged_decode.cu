@@ -46,6 +46,9 @@ namespace {
 #ifndef KLLM_DEC_STAGES
 #define KLLM_DEC_STAGES 2       // bulk-copy ring depth per warp
 #endif
+#ifndef KLLM_MERGE_FLY
+#define KLLM_MERGE_FLY 16       // wide merge: pieces in flight per warp
+#endif
 #ifndef KLLM_DEC_MIN_CTAS_MX
 #define KLLM_DEC_MIN_CTAS_MX 4  // resident MX decode CTAs per SM (register cap)
 #endif
@@ -1207,7 +1210,7 @@ merge_big_kernel(const kllm_decode_args a, float unbias)
 	const long long T = lh->T, W = lh->W;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	constexpr int NV = D / 32;
-	constexpr int kFly = 8;   // pieces in flight per warp
+	constexpr int kFly = KLLM_MERGE_FLY;   // pieces in flight per warp
 	const long long pairs = (long long)count * a.group;
 
 	for (long long pr = blockIdx.x; pr < pairs; pr += gridDim.x) {
